@@ -1,0 +1,301 @@
+"""ctypes front end of the CPU oracle (oracle/mp_oracle.c) — TEST INFRASTRUCTURE ONLY.
+
+Imported by tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg,
+as the checker. The CUDA product path (math-plus_b200/) never imports it.
+
+Each function names the reference function it restates (paths inside the
+math-plus repository); the arithmetic lives in mp_oracle.c.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+
+def build() -> str:
+    """Compile liboracle.so with the committed Makefile (idempotent)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(
+            os.path.join(_HERE, "mp_oracle.c")
+        ):
+            build()
+        L = C.CDLL(_LIB_PATH)
+        f64, f32p, u64 = C.c_double, C.POINTER(C.c_float), C.c_uint64
+        vp, sz, i64p = C.c_void_p, C.c_size_t, C.POINTER(C.c_int64)
+        L.mp_rng_init.argtypes = [vp, u64, u64]
+        L.mp_rng_next_u32.argtypes = [vp]
+        L.mp_rng_next_u32.restype = C.c_uint32
+        L.mp_rng_next_float.argtypes = [vp]
+        L.mp_rng_next_float.restype = f64
+        L.mp_rng_next_below.argtypes = [vp, C.c_uint32]
+        L.mp_rng_next_below.restype = C.c_uint32
+        L.mp_normal_sample.argtypes = [vp, f64, f64]
+        L.mp_normal_sample.restype = f64
+        L.mp_fill_uniform_f32.argtypes = [u64, sz, f64, f64, vp]
+        L.mp_fill_normal_f32.argtypes = [u64, sz, f64, f64, vp]
+        L.mp_fill_normal_half.argtypes = [u64, sz, f64, f64, C.c_int, vp]
+        L.mp_fill_below_i32.argtypes = [u64, sz, C.c_uint32, vp]
+        L.mp_encode_half.argtypes = [C.c_int, f64]
+        L.mp_encode_half.restype = C.c_uint16
+        L.mp_decode_half.argtypes = [C.c_int, C.c_uint16]
+        L.mp_decode_half.restype = f64
+        L.mp_lcg_gemm.argtypes = [sz, C.c_uint32, vp]
+        L.mp_lcg_seeded.argtypes = [sz, C.c_uint32, f64, f64, vp]
+        for n in ("mp_erf", "mp_erfc", "mp_gelu_erf"):
+            getattr(L, n).argtypes = [f64]
+            getattr(L, n).restype = f64
+        L.mp_gemm_nt.argtypes = [vp, vp, vp, sz, sz, C.c_int, C.c_int, C.c_int]
+        L.mp_gemm_nt_par.argtypes = [vp, vp, vp, sz, sz, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.mp_softmax_axis_f32.argtypes = [vp, C.c_int, C.c_int, C.c_int, vp]
+        L.mp_matmul_f32.argtypes = [vp, i64p, C.c_int, vp, i64p, C.c_int, vp, C.c_int]
+        L.mp_matmul_f32.restype = C.c_int
+        L.mp_linear_f32.argtypes = [vp, C.c_int, C.c_int, vp, C.c_int, vp, vp, C.c_int]
+        L.mp_attention_f32.argtypes = [vp, vp, vp] + [C.c_int] * 7 + [f64, vp, C.c_int, i64p, vp, C.c_int]
+        L.mp_layer_norm_f32.argtypes = [vp, C.c_int, C.c_int, vp, vp, f64, vp]
+        L.mp_gelu_f32.argtypes = [vp, sz, vp]
+        L.mp_take_rows_f32.argtypes = [vp, C.c_int, C.c_int, vp, sz, vp]
+        L.mp_take_rows_f32.restype = C.c_long
+        _lib = L
+    return _lib
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def default_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+# ---- seeded inputs (packages/tensor-core/src/random.ts) ---------------------------------
+
+class Rng:
+    """PCG32 XSH-RR, ``new Rng(seed, sequence)`` (random.ts:17-66)."""
+
+    def __init__(self, seed: int = 0, sequence: int = 1):
+        self._st = (C.c_uint64 * 2)()
+        lib().mp_rng_init(C.byref(self._st), seed & (2**64 - 1), sequence & (2**64 - 1))
+
+    def next_uint32(self) -> int:
+        return lib().mp_rng_next_u32(C.byref(self._st))
+
+    def next_float(self) -> float:
+        return lib().mp_rng_next_float(C.byref(self._st))
+
+    def next_below(self, bound: int) -> int:
+        return lib().mp_rng_next_below(C.byref(self._st), bound)
+
+    def normal(self, mean: float = 0.0, std: float = 1.0) -> float:
+        return lib().mp_normal_sample(C.byref(self._st), mean, std)
+
+
+def uniform_f32(n: int, seed: int, lo: float = 0.0, hi: float = 1.0) -> np.ndarray:
+    """``random.uniform([n], {rng: seed(seed), min: lo, max: hi})`` in f32 storage."""
+    out = np.empty(n, np.float32)
+    lib().mp_fill_uniform_f32(seed, n, lo, hi, _ptr(out))
+    return out
+
+
+def normal_f32(n: int, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().mp_fill_normal_f32(seed, n, mean, std, _ptr(out))
+    return out
+
+
+def normal_half_bits(n: int, seed: int, mean: float, std: float, bf16: bool) -> np.ndarray:
+    """``random.normal`` into f16/bf16 storage: Box-Muller then encodeHalf (RNE), as uint16 bits."""
+    out = np.empty(n, np.uint16)
+    lib().mp_fill_normal_half(seed, n, mean, std, 1 if bf16 else 0, _ptr(out))
+    return out
+
+
+def randint_i32(n: int, seed: int, bound: int) -> np.ndarray:
+    out = np.empty(n, np.int32)
+    lib().mp_fill_below_i32(seed, n, bound, _ptr(out))
+    return out
+
+
+def encode_half(x: float, bf16: bool) -> int:
+    return lib().mp_encode_half(1 if bf16 else 0, float(x))
+
+
+def decode_half(bits: int, bf16: bool) -> float:
+    return lib().mp_decode_half(1 if bf16 else 0, bits)
+
+
+def half_bits_to_f32(bits: np.ndarray, bf16: bool) -> np.ndarray:
+    """Exact widening of f16/bf16 bit patterns (tensor-cpu's fromHost, packages/tensor-cpu/src/index.ts:226-229)."""
+    bits = np.ascontiguousarray(bits, dtype=np.uint16)
+    if bf16:
+        return (bits.astype(np.uint32) << 16).view(np.float32)
+    return bits.view(np.float16).astype(np.float32)
+
+
+def lcg_gemm(n: int, seed: int) -> np.ndarray:
+    """packages/tensor-webgpu/test/gemm.test.ts:85-93."""
+    out = np.empty(n, np.float32)
+    lib().mp_lcg_gemm(n, seed & 0xFFFFFFFF, _ptr(out))
+    return out
+
+
+def lcg_seeded(n: int, seed: int, lo: float = -2.0, hi: float = 2.0) -> np.ndarray:
+    """packages/tensor-cpu/test/helpers.ts:115-124 (f64 values)."""
+    out = np.empty(n, np.float64)
+    lib().mp_lcg_seeded(n, seed & 0xFFFFFFFF, lo, hi, _ptr(out))
+    return out
+
+
+# ---- special functions (packages/special/src/index.ts) ----------------------------------
+
+def erf(x: float) -> float:
+    return lib().mp_erf(float(x))
+
+
+def erfc(x: float) -> float:
+    return lib().mp_erfc(float(x))
+
+
+def gelu_erf(x: float) -> float:
+    return lib().mp_gelu_erf(float(x))
+
+
+# ---- ops (tensor-cpu Backend glue over tensor-core kernels) ---------------------------
+
+def matmul(a, b, threads: int = 1) -> np.ndarray:
+    """``CpuBackendImpl.matmul`` -> ``Tensor.matmul`` (tensor-cpu/src/index.ts:755-762)."""
+    a, b = _f32(a), _f32(b)
+    if a.ndim < 2 or b.ndim < 2:
+        raise ValueError("matmul needs rank >= 2")
+    batch = np.broadcast_shapes(a.shape[:-2], b.shape[:-2])
+    out = np.empty(batch + (a.shape[-2], b.shape[-1]), np.float32)
+    sa = (C.c_int64 * a.ndim)(*a.shape)
+    sb = (C.c_int64 * b.ndim)(*b.shape)
+    rc = lib().mp_matmul_f32(_ptr(a), sa, a.ndim, _ptr(b), sb, b.ndim, _ptr(out), threads)
+    if rc != 0:
+        raise ValueError(f"matmul shapes {a.shape} @ {b.shape} (code {rc})")
+    return out
+
+
+def linear(x, w, bias=None, threads: int = 1) -> np.ndarray:
+    """``CpuBackendImpl.linear`` -> ``linearNT`` (tensor-cpu/src/index.ts:764-774)."""
+    x, w = _f32(x), _f32(w)
+    n, k = w.shape
+    rows = x.size // k if k else int(np.prod(x.shape[:-1]))
+    out = np.empty(x.shape[:-1] + (n,), np.float32)
+    bias_keep = _f32(bias) if bias is not None else None
+    lib().mp_linear_f32(_ptr(x), rows, k, _ptr(w), n, _ptr(bias_keep) if bias_keep is not None else None,
+                        _ptr(out), threads)
+    return out
+
+
+def sdpa(q, k, v, mask=None, scale: float | None = None, threads: int = 1) -> np.ndarray:
+    """``CpuBackendImpl.sdpa`` -> ``attention`` (tensor-cpu/src/index.ts:821-840)."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    B, H, Lq, Dh = q.shape
+    Hk, Lk, Dv = k.shape[1], k.shape[2], v.shape[3]
+    if H % Hk:
+        raise ValueError("H must be a multiple of Hk")
+    if scale is None:
+        scale = 1.0 / np.sqrt(Dh)
+    out = np.empty((B, H, Lq, Dv), np.float32)
+    strides = (C.c_int64 * 4)(0, 0, 0, 0)
+    kind, mptr, keep = 0, None, None
+    if mask is not None:
+        m = np.asarray(mask)
+        shape = (1,) * (4 - m.ndim) + m.shape
+        target = (B, H, Lq, Lk)
+        if np.broadcast_shapes(shape, target) != target:
+            raise ValueError(f"mask {m.shape} does not broadcast to {target}")
+        if m.dtype == np.bool_ or m.dtype == np.uint8:
+            keep = np.ascontiguousarray(m != 0, dtype=np.uint8).reshape(shape)
+            kind = 1
+        else:
+            keep = _f32(m).reshape(shape)
+            kind = 2
+        st, acc = [0] * 4, 1
+        for d in range(3, -1, -1):
+            st[d] = 0 if shape[d] == 1 else acc
+            acc *= shape[d]
+        strides = (C.c_int64 * 4)(*st)
+        mptr = _ptr(keep)
+    lib().mp_attention_f32(_ptr(q), _ptr(k), _ptr(v), B, H, Hk, Lq, Lk, Dh, Dv, float(scale), mptr, kind,
+                           strides, _ptr(out), threads)
+    return out
+
+
+def softmax(x, axis: int = -1) -> np.ndarray:
+    """``CpuBackendImpl.softmax`` -> ``softmaxAxis`` (tensor-cpu/src/index.ts:716-722)."""
+    x = _f32(x)
+    axis = axis % x.ndim
+    outer = int(np.prod(x.shape[:axis]))
+    dim = x.shape[axis]
+    inner = int(np.prod(x.shape[axis + 1:]))
+    out = np.empty_like(x)
+    if dim > 0:
+        lib().mp_softmax_axis_f32(_ptr(x), outer, dim, inner, _ptr(out))
+    return out
+
+
+def gelu(x) -> np.ndarray:
+    """``CpuBackendImpl.gelu`` -> ``unaryFlat(UN_GELU)`` (nn-kernels.ts:47)."""
+    x = _f32(x)
+    out = np.empty_like(x)
+    lib().mp_gelu_f32(_ptr(x), x.size, _ptr(out))
+    return out
+
+
+def add_f32(x, y) -> np.ndarray:
+    """Broadcasting f32 add with one f32 rounding (binaryFlat OP_ADD, kernels.ts:43-55)."""
+    return (_f32(x).astype(np.float64) + _f32(y).astype(np.float64)).astype(np.float32)
+
+
+def layer_norm(x, w=None, b=None, eps: float = 1e-5) -> np.ndarray:
+    """``CpuBackendImpl.layerNorm`` -> ``layerNormRows`` (tensor-cpu/src/index.ts:776-782)."""
+    x = _f32(x)
+    D = x.shape[-1]
+    out = np.empty_like(x)
+    wk = _f32(w) if w is not None else None
+    bk = _f32(b) if b is not None else None
+    lib().mp_layer_norm_f32(_ptr(x), x.size // D if D else 0, D, _ptr(wk) if wk is not None else None,
+                            _ptr(bk) if bk is not None else None, eps, _ptr(out))
+    return out
+
+
+def embedding(table, ids) -> np.ndarray:
+    """``CpuBackendImpl.embedding`` -> ``takeRows`` (tensor-cpu/src/index.ts:784-791)."""
+    table = _f32(table)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    V, D = table.shape
+    out = np.empty(ids.shape + (D,), np.float32)
+    bad = lib().mp_take_rows_f32(_ptr(table), D, V, _ptr(ids), ids.size, _ptr(out))
+    if bad >= 0:
+        raise IndexError(f"takeRows: row index {int(ids.reshape(-1)[bad])} out of range [0, {V})")
+    return out
+
+
+def gemm_nt_f64(a: np.ndarray, b_nt: np.ndarray, threads: int = 1) -> np.ndarray:
+    """Raw ``gemmNT`` over packed f64 panels (kernels.ts:299-362): a [M,K], b_nt [N,K]."""
+    a = np.ascontiguousarray(a, np.float64)
+    b_nt = np.ascontiguousarray(b_nt, np.float64)
+    M, K = a.shape
+    N = b_nt.shape[0]
+    out = np.empty((M, N), np.float64)
+    lib().mp_gemm_nt_par(_ptr(a), _ptr(b_nt), _ptr(out), 0, N, M, N, K, threads)
+    return out
