@@ -1,0 +1,195 @@
+/*
+ * libmathplus_cuda.so — the C ABI of the math-plus CUDA device backend (B200, sm_100a).
+ *
+ * This is the boundary a math-plus device facade binds (Node-API, Deno.dlopen, bun:ffi or
+ * Python ctypes): plain pointers, sizes in bytes or elements, C linkage, an int status on
+ * every call and no C++ or torch types. It replaces, for the GEMM / attention path, what the
+ * WebGPU runtime does under packages/tensor-webgpu (the external @johnhenry/backend-webgpu
+ * kernels) and what tensor-cpu's Backend does on the host:
+ *
+ *   mpc_gemm   <- Backend.matmul / Backend.linear   (packages/tensor-cpu/src/index.ts:755-774)
+ *   mpc_sdpa   <- Backend.sdpa                      (packages/tensor-cpu/src/index.ts:821-840)
+ *   mpc_softmax, mpc_gelu, mpc_add, mpc_layer_norm, mpc_embedding, mpc_cast
+ *              <- Backend.softmax/gelu/add/layerNorm/embedding/cast (index.ts:598, 716-722, 776-791, 406-425)
+ *   mpc_memcpy_h2d_async / mpc_memcpy_d2h_async
+ *              <- Backend.fromHost / Backend.read   (packages/tensor-cpu/src/index.ts:216-260)
+ *
+ * Conventions (kept from the reference's native FFI, crates/tensor-wasm-kernels/src/lib.rs:17-38
+ * and packages/tensor-wasm/src/native.ts:96-104): every call returns an mpc_status and never
+ * aborts; a failed call leaves a message for mpc_last_error(); strides and offsets are in
+ * ELEMENTS; a NULL stream means the device's own stream.
+ */
+#ifndef MATHPLUS_CUDA_H
+#define MATHPLUS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default) /* the library builds with hidden visibility; export only this API */
+#endif
+
+#define MPC_ABI_VERSION 1
+
+typedef enum {
+  MPC_OK = 0,
+  MPC_ERR_INVALID = 1,     /* bad argument: shape, stride, dtype, null pointer */
+  MPC_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
+  MPC_ERR_OOM = 3,         /* device allocation failed (or the allocator cap was reached) */
+  MPC_ERR_CUDA = 4,        /* a CUDA runtime / driver call failed */
+  MPC_ERR_TIMEOUT = 5,     /* a kernel's bounded wait ran out; the kernel returned early */
+  MPC_ERR_POISONED = 6,    /* an earlier fault poisoned this device handle: destroy it */
+  MPC_ERR_NO_DEVICE = 7,   /* no CUDA device / not an sm_100 device */
+  MPC_ERR_COMM = 8         /* NCCL unavailable or a collective failed */
+} mpc_status;
+
+typedef enum { MPC_F32 = 0, MPC_F16 = 1, MPC_BF16 = 2, MPC_I32 = 3, MPC_BOOL = 4 } mpc_dtype;
+
+typedef struct mpc_device mpc_device; /* one per CUDA device ordinal and process */
+typedef void *mpc_stream;             /* a cudaStream_t; NULL = the device's own stream */
+typedef void *mpc_event;              /* a cudaEvent_t */
+typedef struct mpc_comm mpc_comm;     /* an NCCL communicator (one rank of a group) */
+
+typedef struct {
+  char name[128];
+  int ordinal;
+  int cc_major, cc_minor;
+  int sm_count;
+  size_t total_bytes;
+  size_t smem_per_block_optin;
+  int runtime_version, driver_version;
+} mpc_device_info_t;
+
+/* ---- device and errors (no reference counterpart beyond createWebGpuDevice,
+ *      packages/tensor-webgpu/src/facade.ts:52-64, and detectWebGPU, src/device.ts:87-121) */
+int mpc_version(void);
+int mpc_device_count(int *count);
+int mpc_device_create(int ordinal, unsigned flags, mpc_device **dev);
+int mpc_device_destroy(mpc_device *dev);
+int mpc_device_info(mpc_device *dev, mpc_device_info_t *info);
+/* Thread-local message of the last failed call on this thread (dev may be NULL). */
+const char *mpc_last_error(mpc_device *dev);
+/* Status of the device handle: MPC_OK, or the sticky MPC_ERR_POISONED / MPC_ERR_TIMEOUT. */
+int mpc_device_status(mpc_device *dev);
+/* Limit for every in-kernel bounded wait (nanoseconds; 0 restores the default). */
+int mpc_set_wait_timeout_ns(mpc_device *dev, uint64_t ns);
+/* Clears a recorded MPC_ERR_TIMEOUT once the caller has handled it (not a poisoned handle). */
+int mpc_device_clear_error(mpc_device *dev);
+/* Failure-path self test: launches one wait on an mbarrier nothing releases, with the given
+ * limit; returns MPC_ERR_TIMEOUT once the kernel has given up and returned (the context stays
+ * usable; clear it with mpc_device_clear_error). No fault, trap or hang is involved. */
+int mpc_selftest_wait_timeout(mpc_device *dev, uint64_t timeout_ns);
+
+/* ---- memory: a caching allocator per device (Backend.fromHost's one copy, index.ts:225) */
+int mpc_alloc(mpc_device *dev, size_t bytes, void **ptr);
+int mpc_free(mpc_device *dev, void *ptr);
+/* Cap on bytes handed out by mpc_alloc (0 = no cap): lets tests inject allocation failure. */
+int mpc_set_alloc_limit(mpc_device *dev, size_t bytes);
+int mpc_alloc_stats(mpc_device *dev, size_t *in_use, size_t *cached);
+int mpc_trim(mpc_device *dev);
+int mpc_host_alloc(mpc_device *dev, size_t bytes, void **ptr); /* pinned host memory */
+int mpc_host_free(mpc_device *dev, void *ptr);
+int mpc_memcpy_h2d_async(mpc_device *dev, void *dst, const void *src, size_t bytes, mpc_stream s);
+int mpc_memcpy_d2h_async(mpc_device *dev, void *dst, const void *src, size_t bytes, mpc_stream s);
+int mpc_memcpy_d2d_async(mpc_device *dev, void *dst, const void *src, size_t bytes, mpc_stream s);
+int mpc_memset_async(mpc_device *dev, void *dst, int value, size_t bytes, mpc_stream s);
+
+/* ---- streams and events (the GPU profiler of backend-webgpu, packages/tensor-webgpu/README.md:111-115) */
+int mpc_stream_create(mpc_device *dev, mpc_stream *s);
+int mpc_stream_destroy(mpc_device *dev, mpc_stream s);
+int mpc_stream_sync(mpc_device *dev, mpc_stream s);
+int mpc_device_stream(mpc_device *dev, mpc_stream *s);
+int mpc_event_create(mpc_device *dev, mpc_event *e);
+int mpc_event_destroy(mpc_device *dev, mpc_event e);
+int mpc_event_record(mpc_device *dev, mpc_event e, mpc_stream s);
+int mpc_event_elapsed_ms(mpc_device *dev, mpc_event start, mpc_event stop, float *ms);
+/* Waits for all work of the device, then reports any kernel-side error word. */
+int mpc_sync(mpc_device *dev);
+/* Number of this library's kernels launched on the device so far. */
+int mpc_launch_count(mpc_device *dev, uint64_t *count);
+
+/* ---- GEMM: C = epilogue(alpha * A·B) ------------------------------------------------------
+ * Replaces Backend.matmul (B is [K,N]; packages/tensor-cpu/src/index.ts:755-762 ->
+ * Tensor.matmul, packages/tensor-core/src/index.ts:1584-1730) and Backend.linear (B is a
+ * PyTorch [N,K] weight plus bias; index.ts:764-774 -> linearNT, nn-kernels.ts:74-101), and the
+ * DeviceArray chain matmul -> add(bias) -> gelu fused into one kernel.
+ * f16 / bf16 inputs run on tcgen05 (f32 accumulation); f32 inputs run 3xTF32 on tcgen05.
+ * A is [batch.., M, K] and C is [batch, M, N], both row-major; bias is f32 [N]. */
+enum { MPC_EPI_BIAS = 1, MPC_EPI_GELU = 2 };
+enum { MPC_B_KN = 0, MPC_B_NK = 1 };
+typedef struct {
+  int64_t m, n, k;
+  int32_t dtype_in;   /* MPC_F32, MPC_F16 or MPC_BF16 (A and B alike) */
+  int32_t dtype_out;  /* MPC_F32, MPC_F16 or MPC_BF16 */
+  int32_t b_layout;   /* MPC_B_KN (matmul) or MPC_B_NK (linear) */
+  int32_t epilogue;   /* MPC_EPI_* flags */
+  float alpha;        /* scale applied to A·B before the bias */
+  int32_t batch_rank; /* 0..4 batch axes, output batch shape below (C-contiguous) */
+  int64_t batch_shape[4];
+  int64_t a_batch_stride[4]; /* element strides of A / B per batch axis; 0 = broadcast */
+  int64_t b_batch_stride[4];
+} mpc_gemm_desc;
+int mpc_gemm(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B, void *C,
+             const float *bias, mpc_stream s);
+
+/* ---- fused scaled-dot-product attention ----------------------------------------------------
+ * softmax(scale * Q·Kᵀ + mask) · V over Q [B,H,Lq,D], K [B,Hk,Lk,D], V [B,Hk,Lk,Dv] into
+ * O [B,H,Lq,Dv] (all contiguous), H a multiple of Hk (grouped-query heads share K/V).
+ * Replaces Backend.sdpa (packages/tensor-cpu/src/index.ts:821-840 -> attention,
+ * packages/tensor-core/src/nn-kernels.ts:179-239). causal = 1 hides key j from query i when
+ * j > i (the [Lq,Lk] lower-triangular bool mask of the reference tests). A query row with no
+ * visible key yields zeros (nn-kernels.ts:222-225). LSE (optional, f32 [B,H,Lq]) receives the
+ * natural-log softmax normaliser of each row (-inf for a fully masked row). */
+enum { MPC_MASK_NONE = 0, MPC_MASK_BOOL = 1, MPC_MASK_ADD = 2 };
+typedef struct {
+  int64_t b, h, hk, lq, lk, d, dv;
+  int32_t dtype;     /* MPC_F16 / MPC_BF16 (tcgen05 path) or MPC_F32 (CUDA-core path); O has this dtype */
+  int32_t causal;
+  float scale;
+  int32_t mask_kind; /* MPC_MASK_* ; mask is u8 (bool) or f32 (additive) */
+  int64_t mask_strides[4]; /* element strides aligned to [B,H,Lq,Lk]; 0 = broadcast */
+} mpc_sdpa_desc;
+int mpc_sdpa(mpc_device *dev, const mpc_sdpa_desc *desc, const void *Q, const void *K, const void *V,
+             const void *mask, void *O, float *LSE, mpc_stream s);
+
+/* ---- the element-wise / row ops the GEMM and attention path touches ------------------------ */
+/* softmax along the middle axis of a contiguous [outer, dim, inner] block, f32 out
+ * (Backend.softmax -> softmaxAxis, packages/tensor-core/src/kernels.ts:219-247). */
+int mpc_softmax(mpc_device *dev, const void *x, int32_t dtype, float *out, int64_t outer, int64_t dim,
+                int64_t inner, mpc_stream s);
+/* exact-erf GELU (Backend.gelu -> geluErf, packages/special/src/index.ts:191-193). */
+int mpc_gelu(mpc_device *dev, const void *x, int32_t dtype_in, void *out, int32_t dtype_out, int64_t n,
+             mpc_stream s);
+/* out = x + y with y broadcast as a [rows_y, n] block repeated (rows_y = 1 for a bias row)
+ * (Backend.add, packages/tensor-cpu/src/device-array.ts:289-291). */
+int mpc_add(mpc_device *dev, const void *x, const void *y, void *out, int32_t dtype, int64_t n_x,
+            int64_t n_y, mpc_stream s);
+/* LayerNorm over the last axis (Backend.layerNorm -> layerNormRows, nn-kernels.ts:108-129). */
+int mpc_layer_norm(mpc_device *dev, const void *x, int32_t dtype_in, const float *weight, const float *bias,
+                   float eps, void *out, int32_t dtype_out, int64_t rows, int64_t d, mpc_stream s);
+/* Row gather (Backend.embedding -> takeRows, nn-kernels.ts:277-286). An out-of-range id
+ * returns MPC_ERR_INVALID after the call (the offending position goes to *bad_index). */
+int mpc_embedding(mpc_device *dev, const void *table, int32_t dtype, const int32_t *ids, void *out,
+                  int64_t n_ids, int64_t rows, int64_t d, int64_t *bad_index, mpc_stream s);
+/* Element type conversion f32 <-> f16 / bf16, RNE (Backend.cast, index.ts:406-425). */
+int mpc_cast(mpc_device *dev, const void *x, int32_t dtype_in, void *out, int32_t dtype_out, int64_t n,
+             mpc_stream s);
+
+/* ---- multi-GPU: NCCL over NVLink, one rank per process (no reference counterpart) ---------- */
+int mpc_comm_unique_id(void *id128);
+int mpc_comm_init(mpc_device *dev, int nranks, int rank, const void *id128, mpc_comm **comm);
+int mpc_comm_destroy(mpc_comm *comm);
+int mpc_comm_abort(mpc_comm *comm);
+/* Gathers `bytes` from every rank into recv (rank r's block at offset r*bytes). */
+int mpc_allgather(mpc_comm *comm, const void *send, void *recv, size_t bytes, mpc_stream s);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+#endif

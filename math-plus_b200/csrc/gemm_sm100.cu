@@ -1,0 +1,619 @@
+// GEMM on the B200 tensor cores (tcgen05 / TMEM / TMA), sm_100a.
+//
+// C[b] = epilogue(alpha * A[b] · B[b]) for the math-plus Backend.matmul / Backend.linear path
+// (packages/tensor-cpu/src/index.ts:755-774; the reference computes it with gemmNT,
+// packages/tensor-core/src/kernels.ts:299-362, in f64 on the host).
+//
+// One persistent CTA per SM, 6 warps, warp-specialised:
+//   warp 0      TMA producer: A / B tiles into a STAGES-deep shared-memory ring (mbarrier full/empty)
+//   warp 1      MMA issuer: one thread issues tcgen05.mma into a TMEM accumulator and commits
+//               stage releases and accumulator completion to mbarriers; also owns the TMEM allocation
+//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32*(w%4)..+31),
+//               apply alpha / +bias / exact-erf GELU, convert, stage 32x128-byte swizzled blocks
+//               in shared memory and TMA-store them (bounds clipped by the tensor map)
+// Two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1.
+//
+// Operand layouts, all with the 128-byte swizzle:
+//   A        K-major (row-major [M,K]); box {BK, 128}
+//   B [N,K]  K-major (the linear weight);  box {BK, BN}
+//   B [K,N]  MN-major (the matmul operand); BN/64 boxes {64, BK}, one per 128-byte N chunk
+// f16 / bf16 inputs use kind::f16 (BK = 64, MMA K = 16, BN = 256, 4 stages).
+// f32 inputs use 3xTF32 (kind::tf32, BK = 32, MMA K = 8, BN = 128, 3 stages): a prologue splits each
+// operand into tf32 hi + lo parts (K-major), and the main loop accumulates lo·hi + hi·lo + hi·hi.
+#include <cstdio>
+
+#include "mpc_internal.h"
+#include "sm100.cuh"
+
+namespace mpc {
+namespace gemm {
+
+enum Kind { kHalf = 0, kTF32x3 = 1 };
+
+struct Params {
+  int M, N, K;
+  int tiles_m, tiles_n, tiles_total;
+  int k_blocks;
+  int group_m;
+  int brank;
+  int bshape[4];
+  int a_bstride[4];  // batch strides in whole matrices (0 = broadcast)
+  int b_bstride[4];
+  float alpha;
+  const float *bias;
+  int epilogue;
+  int out_dtype;
+  uint32_t idesc;  // tcgen05 instruction descriptor (operand format, B major, M, N)
+  int *err;
+  unsigned long long timeout_ns;
+};
+
+struct Maps {
+  CUtensorMap a, b, a_lo, b_lo, c;
+};
+
+template <int KIND, bool B_MN, int BN, int STAGES>
+struct Cfg {
+  static constexpr int BM = 128;
+  static constexpr int ES = KIND == kHalf ? 2 : 4;  // operand element bytes
+  static constexpr int BK = 128 / ES;               // elements in one 128-byte row
+  static constexpr int UK = KIND == kHalf ? 16 : 8;  // K of one tcgen05.mma
+  static constexpr int KSTEPS = BK / UK;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int NOPS = KIND == kHalf ? 1 : 2;
+  static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
+  static constexpr int EPI_BYTES = 4 * 2 * 4096;  // 4 warps x 2 buffers x (32 rows x 128 B)
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert(!(KIND == kTF32x3 && B_MN), "3xTF32 operands are always K-major");
+};
+
+__device__ __forceinline__ void tile_coords(const Params &p, int tile, int &b, int &mt, int &nt) {
+  const int per_batch = p.tiles_m * p.tiles_n;
+  b = tile / per_batch;
+  const int r = tile - b * per_batch;
+  const int group = p.group_m * p.tiles_n;
+  const int g = r / group;
+  const int first_m = g * p.group_m;
+  const int gm = min(p.tiles_m - first_m, p.group_m);
+  const int rg = r - g * group;
+  mt = first_m + rg % gm;
+  nt = rg / gm;
+}
+
+__device__ __forceinline__ void batch_index(const Params &p, int b, int &ia, int &ib) {
+  ia = 0;
+  ib = 0;
+  for (int d = p.brank - 1; d >= 0; --d) {
+    const int i = b % p.bshape[d];
+    b /= p.bshape[d];
+    ia += i * p.a_bstride[d];
+    ib += i * p.b_bstride[d];
+  }
+}
+
+__device__ __forceinline__ float gelu_erf_f32(float x) {
+  // exact GELU x·Φ(x) = 0.5·x·erfc(-x/√2)  (packages/special/src/index.ts:186-193)
+  return 0.5f * x * erfcf(-x * 0.70710678118654752f);
+}
+
+// One 128-byte-per-row output chunk (32 f32 or 64 half columns) of this warp's 32 rows.
+template <int OUT>
+__device__ __forceinline__ void epilogue_chunk(const Params &p, const CUtensorMap *cmap, uint8_t *buf,
+                                               const uint32_t (&r0)[32], const uint32_t (&r1)[32], int col0,
+                                               int row0, int b, int lane) {
+  constexpr int CPC = OUT == MPC_F32 ? 32 : 64;
+  float f[CPC];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r0[j]);
+  if constexpr (CPC == 64) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[32 + j] = __uint_as_float(r1[j]);
+  }
+  if (p.alpha != 1.0f) {
+#pragma unroll
+    for (int j = 0; j < CPC; ++j) f[j] *= p.alpha;
+  }
+  if (p.epilogue & MPC_EPI_BIAS) {
+#pragma unroll
+    for (int h = 0; h < CPC / 32; ++h) {
+      const int c = col0 + h * 32 + lane;
+      const float bl = c < p.N ? __ldg(p.bias + c) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[h * 32 + j] += __shfl_sync(0xffffffffu, bl, j);
+    }
+  }
+  if (p.epilogue & MPC_EPI_GELU) {
+#pragma unroll
+    for (int j = 0; j < CPC; ++j) f[j] = gelu_erf_f32(f[j]);
+  }
+  // Row `lane` of the 32x128-byte block, 16-byte chunk j stored at chunk (j ^ (lane & 7)):
+  // the 128-byte swizzle the store map expects, and conflict-free for these writes.
+  uint8_t *row = buf + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 v;
+    if constexpr (OUT == MPC_F32) {
+      v = make_uint4(__float_as_uint(f[4 * j]), __float_as_uint(f[4 * j + 1]), __float_as_uint(f[4 * j + 2]),
+                     __float_as_uint(f[4 * j + 3]));
+    } else {
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if constexpr (OUT == MPC_BF16) {
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(f[8 * j + 2 * e], f[8 * j + 2 * e + 1]);
+          w[e] = *reinterpret_cast<uint32_t *>(&h2);
+        } else {
+          __half2 h2 = __floats2half2_rn(f[8 * j + 2 * e], f[8 * j + 2 * e + 1]);
+          w[e] = *reinterpret_cast<uint32_t *>(&h2);
+        }
+      }
+      v = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) = v;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && row0 < p.M && col0 < p.N) {
+    tma_store_3d(cmap, buf, col0, row0, b);
+  }
+  if (lane == 0) tma_store_commit();
+}
+
+template <int KIND, bool B_MN, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
+  using C = Cfg<KIND, B_MN, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *stages = smem;
+  uint8_t *epi = smem + STAGES * C::STAGE_BYTES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(epi + C::EPI_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *acc_full = empty + STAGES;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *drain = acc_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&maps.a);
+    tma_prefetch_desc(&maps.b);
+    tma_prefetch_desc(&maps.c);
+    if constexpr (KIND == kTF32x3) {
+      tma_prefetch_desc(&maps.a_lo);
+      tma_prefetch_desc(&maps.b_lo);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.tiles_total; tile += gridDim.x) {
+        int b, mt, nt, ia, ib;
+        tile_coords(p, tile, b, mt, nt);
+        batch_index(p, b, ia, ib);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitProducer, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sa = stages + stage * C::STAGE_BYTES;
+          uint8_t *sb = sa + C::A_BYTES;
+          mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_3d(&maps.a, &full[stage], sa, kb * C::BK, mt * C::BM, ia);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(&maps.b, &full[stage], sb + j * (C::BK * 128), nt * BN + j * 64, kb * C::BK, ib);
+          } else {
+            tma_load_3d(&maps.b, &full[stage], sb, kb * C::BK, nt * BN, ib);
+          }
+          if constexpr (KIND == kTF32x3) {
+            uint8_t *sa2 = sb + C::B_BYTES;
+            uint8_t *sb2 = sa2 + C::A_BYTES;
+            tma_load_3d(&maps.a_lo, &full[stage], sa2, kb * C::BK, mt * C::BM, ia);
+            tma_load_3d(&maps.b_lo, &full[stage], sb2, kb * C::BK, nt * BN, ib);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already in flight land before shared memory goes away: wait on the
+        // full barriers of the (up to STAGES) most recently armed slots.
+        const int n = issued < STAGES ? issued : STAGES;
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < n; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          volatile int never = 0;
+          mbar_wait(&full[s], ph, &never, p.err, kErrWaitProducer, p.timeout_ns);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (one thread) ----------------
+    if (lane == 0) {
+      const uint32_t idesc_rt = p.idesc;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < p.tiles_total; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.err, kErrWaitAccEmpty, p.timeout_ns)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(stages + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < C::KSTEPS; ++ks) {
+            const uint64_t ad = make_sdesc(a_addr + ks * (C::UK * C::ES), 16, 1024);
+            const uint64_t bd = B_MN ? make_sdesc(b_addr + ks * (C::UK * 128), C::BK * 128, 1024)
+                                     : make_sdesc(b_addr + ks * (C::UK * C::ES), 16, 1024);
+            const uint32_t accum = (kb | ks) ? 1u : 0u;
+            if constexpr (KIND == kHalf) {
+              mma_f16_ss(d_tmem, ad, bd, idesc_rt, accum);
+            } else {
+              const uint32_t a2 = b_addr + C::B_BYTES;
+              const uint32_t b2 = a2 + C::A_BYTES;
+              const uint64_t ad2 = make_sdesc(a2 + ks * (C::UK * C::ES), 16, 1024);
+              const uint64_t bd2 = make_sdesc(b2 + ks * (C::UK * C::ES), 16, 1024);
+              mma_tf32_ss(d_tmem, ad2, bd, idesc_rt, accum);  // lo · hi
+              mma_tf32_ss(d_tmem, ad, bd2, idesc_rt, 1u);     // hi · lo
+              mma_tf32_ss(d_tmem, ad, bd, idesc_rt, 1u);      // hi · hi
+            }
+          }
+          tc_commit(&empty[stage]);  // the slot is free once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[acc]);
+      }
+      // Every MMA this thread issued has completed once `drain` flips.
+      tc_commit(drain);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never, p.err, kErrWaitConsumer, p.timeout_ns);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    uint8_t *stg = epi + (warp - 2) * 8192;
+    int local = 0, stores = 0;
+    for (int tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++local) {
+      int b, mt, nt;
+      tile_coords(p, tile, b, mt, nt);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull, p.timeout_ns)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const int row0 = mt * C::BM + q * 32;
+      const int cpc = p.out_dtype == MPC_F32 ? 32 : 64;
+      const int nchunks = BN / cpc;
+      for (int c = 0; c < nchunks; ++c) {
+        uint32_t r0[32], r1[32];
+        tmem_ld32(t_row + c * cpc, r0);
+        if (cpc == 64) tmem_ld32(t_row + c * cpc + 32, r1);
+        tmem_ld_wait();
+        if (c == nchunks - 1) {
+          // Accumulator fully read: hand it back to the MMA warp before the math and stores.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+        }
+        uint8_t *buf = stg + (stores & 1) * 4096;
+        if (lane == 0) tma_store_wait_read<1>();  // the store issued from this buffer 2 chunks ago has read it
+        __syncwarp();
+        const int col0 = nt * BN + c * cpc;
+        if (p.out_dtype == MPC_F32)
+          epilogue_chunk<MPC_F32>(p, &maps.c, buf, r0, r1, col0, row0, b, lane);
+        else if (p.out_dtype == MPC_BF16)
+          epilogue_chunk<MPC_BF16>(p, &maps.c, buf, r0, r1, col0, row0, b, lane);
+        else
+          epilogue_chunk<MPC_F16>(p, &maps.c, buf, r0, r1, col0, row0, b, lane);
+        ++stores;
+      }
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---- 3xTF32 prologue: x = hi + lo with hi, lo tf32 values (round to nearest) ----------------
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Row-major [rows, cols] -> [rows, ld] hi / lo (columns cols..ld-1 zero).
+__global__ void split_rows_kernel(const float *__restrict__ src, float *__restrict__ hi, float *__restrict__ lo,
+                                  int64_t rows, int64_t cols, int64_t ld) {
+  const int64_t total = rows * ld;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / ld, c = i - r * ld;
+    const float x = c < cols ? src[r * cols + c] : 0.0f;
+    const float h = to_tf32(x);
+    hi[i] = h;
+    lo[i] = to_tf32(x - h);
+  }
+}
+
+// [nb][K][N] -> [nb][N][ld] hi / lo, transposing through a 32x33 shared tile.
+__global__ void split_transpose_kernel(const float *__restrict__ src, float *__restrict__ hi, float *__restrict__ lo,
+                                       int K, int N, int ld) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  const float *s = src + (int64_t)b * K * N;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int k = k0 + i, n = n0 + threadIdx.x;
+    tile[i][threadIdx.x] = (k < K && n < N) ? s[(int64_t)k * N + n] : 0.0f;
+  }
+  __syncthreads();
+  float *h = hi + (int64_t)b * N * ld;
+  float *l = lo + (int64_t)b * N * ld;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int n = n0 + i, k = k0 + threadIdx.x;
+    if (n < N && k < ld) {
+      const float x = tile[threadIdx.x][i];
+      const float hv = to_tf32(x);
+      h[(int64_t)n * ld + k] = hv;
+      l[(int64_t)n * ld + k] = to_tf32(x - hv);
+    }
+  }
+}
+
+// K == 0: C = epilogue(0).
+__global__ void fill_epilogue_kernel(void *C, int out_dtype, int64_t rows, int64_t N, const float *bias, int epi) {
+  const int64_t total = rows * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = 0.0f;
+    if (epi & MPC_EPI_BIAS) v += bias[i % N];
+    if (epi & MPC_EPI_GELU) v = gelu_erf_f32(v);
+    if (out_dtype == MPC_F32)
+      static_cast<float *>(C)[i] = v;
+    else if (out_dtype == MPC_BF16)
+      static_cast<__nv_bfloat16 *>(C)[i] = __float2bfloat16_rn(v);
+    else
+      static_cast<__half *>(C)[i] = __float2half_rn(v);
+  }
+}
+
+template <int KIND, bool B_MN, int BN, int STAGES>
+int launch(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
+  using C = Cfg<KIND, B_MN, BN, STAGES>;
+  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES>;
+  static bool configured[64] = {};
+  const int ord = dev->ordinal & 63;
+  if (!configured[ord]) {
+    MPC_CUDA(dev, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured[ord] = true;
+  }
+  const int grid = p.tiles_total < dev->prop.multiProcessorCount ? p.tiles_total : dev->prop.multiProcessorCount;
+  kern<<<grid, 192, C::SMEM, st>>>(maps, p);
+  dev->launches++;
+  return check_launch(dev, "gemm_kernel");
+}
+
+}  // namespace gemm
+
+// ---- host entry -----------------------------------------------------------------------------
+static CUtensorMapDataType tmap_dtype(int dt) {
+  switch (dt) {
+    case MPC_F32:
+      return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    case MPC_F16:
+      return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default:
+      return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  }
+}
+
+static inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, void *Cout, const float *bias,
+             cudaStream_t st) {
+  using namespace gemm;
+  const int64_t M = d->m, N = d->n, K = d->k;
+  if (M < 0 || N < 0 || K < 0) return fail(MPC_ERR_INVALID, "mpc_gemm: negative dimension m=%lld n=%lld k=%lld",
+                                           (long long)M, (long long)N, (long long)K);
+  if (d->dtype_in != MPC_F32 && d->dtype_in != MPC_F16 && d->dtype_in != MPC_BF16)
+    return fail(MPC_ERR_INVALID, "mpc_gemm: dtype_in %d is not f32/f16/bf16", d->dtype_in);
+  if (d->dtype_out != MPC_F32 && d->dtype_out != MPC_F16 && d->dtype_out != MPC_BF16)
+    return fail(MPC_ERR_INVALID, "mpc_gemm: dtype_out %d is not f32/f16/bf16", d->dtype_out);
+  if (d->b_layout != MPC_B_KN && d->b_layout != MPC_B_NK)
+    return fail(MPC_ERR_INVALID, "mpc_gemm: b_layout %d", d->b_layout);
+  if (d->batch_rank < 0 || d->batch_rank > 4) return fail(MPC_ERR_INVALID, "mpc_gemm: batch_rank %d", d->batch_rank);
+  if ((d->epilogue & MPC_EPI_BIAS) && !bias) return fail(MPC_ERR_INVALID, "mpc_gemm: BIAS epilogue without bias");
+  if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return fail(MPC_ERR_UNSUPPORTED, "mpc_gemm: dimension above 2^30");
+  int64_t batch = 1, nA = 1, nB = 1;
+  Params p{};
+  p.brank = d->batch_rank;
+  for (int i = 0; i < d->batch_rank; ++i) {
+    const int64_t s = d->batch_shape[i];
+    if (s < 0) return fail(MPC_ERR_INVALID, "mpc_gemm: batch_shape[%d] = %lld", i, (long long)s);
+    batch *= s;
+    const int64_t sa = d->a_batch_stride[i], sb = d->b_batch_stride[i];
+    if (sa < 0 || sb < 0 || (M * K && sa % (M * K)) || (K * N && sb % (K * N)))
+      return fail(MPC_ERR_INVALID, "mpc_gemm: batch strides must be whole matrices (axis %d: %lld, %lld)", i,
+                  (long long)sa, (long long)sb);
+    p.bshape[i] = (int)s;
+    p.a_bstride[i] = M * K ? (int)(sa / (M * K)) : 0;
+    p.b_bstride[i] = K * N ? (int)(sb / (K * N)) : 0;
+    if (s > 0) {
+      nA += (s - 1) * p.a_bstride[i];
+      nB += (s - 1) * p.b_bstride[i];
+    }
+  }
+  if (batch == 0 || M == 0 || N == 0) return MPC_OK;
+  if (!A || !B || !Cout) return fail(MPC_ERR_INVALID, "mpc_gemm: null operand pointer");
+  const size_t eo = dtype_size(d->dtype_out);
+  if (K == 0) {
+    gemm::fill_epilogue_kernel<<<1184, 256, 0, st>>>(Cout, d->dtype_out, batch * M, N, bias, d->epilogue);
+    dev->launches++;
+    return check_launch(dev, "fill_epilogue_kernel");
+  }
+
+  const bool tf32 = d->dtype_in == MPC_F32;
+  const bool b_mn = !tf32 && d->b_layout == MPC_B_KN;
+  const int BN = tf32 ? 128 : 256;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.tiles_m = (int)((M + 127) / 128);
+  p.tiles_n = (int)((N + BN - 1) / BN);
+  const int64_t tiles = batch * p.tiles_m * p.tiles_n;
+  if (tiles > INT32_MAX) return fail(MPC_ERR_UNSUPPORTED, "mpc_gemm: %lld tiles", (long long)tiles);
+  p.tiles_total = (int)tiles;
+  p.k_blocks = (int)((K + (tf32 ? 31 : 63)) / (tf32 ? 32 : 64));
+  p.group_m = 16;
+  p.alpha = d->alpha;
+  p.bias = bias;
+  p.epilogue = d->epilogue & (MPC_EPI_BIAS | MPC_EPI_GELU);
+  p.idesc = make_idesc(tf32 ? kFmtTF32 : (d->dtype_in == MPC_BF16 ? kFmtBF16 : kFmtF16), b_mn, 128, BN);
+  p.out_dtype = d->dtype_out;
+  p.err = dev->d_err;
+  p.timeout_ns = dev->timeout_ns;
+
+  Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  Scratch sa, sb, sa2, sb2, sc;
+  const CUtensorMapSwizzle SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  int rc;
+
+  // Output: a padded staging matrix when the row pitch or base is not 16-byte aligned.
+  void *cdst = Cout;
+  int64_t ldc = N;
+  if (((uintptr_t)Cout & 15) || (N * eo) % 16) {
+    ldc = round_up(N, 16 / eo);
+    if ((rc = sc.get(dev, st, (size_t)(batch * M * ldc) * eo))) return rc;
+    cdst = sc.ptr;
+  }
+  if ((rc = make_map_3d(&maps.c, tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo,
+                        (uint32_t)(128 / eo), 32, SW)))
+    return rc;
+
+  if (tf32) {
+    const int64_t ldk = round_up(K, 4);
+    if ((rc = sa.get(dev, st, (size_t)(nA * M * ldk) * 4)) || (rc = sa2.get(dev, st, (size_t)(nA * M * ldk) * 4)) ||
+        (rc = sb.get(dev, st, (size_t)(nB * N * ldk) * 4)) || (rc = sb2.get(dev, st, (size_t)(nB * N * ldk) * 4)))
+      return rc;
+    split_rows_kernel<<<1184, 256, 0, st>>>(static_cast<const float *>(A), (float *)sa.ptr, (float *)sa2.ptr, nA * M,
+                                            K, ldk);
+    dev->launches++;
+    if (d->b_layout == MPC_B_NK) {
+      split_rows_kernel<<<1184, 256, 0, st>>>(static_cast<const float *>(B), (float *)sb.ptr, (float *)sb2.ptr,
+                                              nB * N, K, ldk);
+    } else {
+      dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)nB);
+      split_transpose_kernel<<<g, dim3(32, 8), 0, st>>>(static_cast<const float *>(B), (float *)sb.ptr,
+                                                         (float *)sb2.ptr, (int)K, (int)N, (int)ldk);
+    }
+    dev->launches++;
+    if ((rc = check_launch(dev, "split_tf32"))) return rc;
+    const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if ((rc = make_map_3d(&maps.a, f32, sa.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
+        (rc = make_map_3d(&maps.a_lo, f32, sa2.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
+        (rc = make_map_3d(&maps.b, f32, sb.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)) ||
+        (rc = make_map_3d(&maps.b_lo, f32, sb2.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)))
+      return rc;
+    rc = launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
+  } else {
+    const size_t es = 2;
+    const CUtensorMapDataType dt = tmap_dtype(d->dtype_in);
+    // A: [nA][M][K]; a padded copy when K*2 bytes is not a multiple of 16 or A is misaligned.
+    const void *ap = A;
+    int64_t lda = K;
+    if (((uintptr_t)A & 15) || (K * es) % 16) {
+      lda = round_up(K, 8);
+      if ((rc = sa.get(dev, st, (size_t)(nA * M * lda) * es))) return rc;
+      MPC_CUDA(dev, cudaMemcpy2DAsync(sa.ptr, lda * es, A, K * es, K * es, nA * M, cudaMemcpyDeviceToDevice, st));
+      ap = sa.ptr;
+    }
+    if ((rc = make_map_3d(&maps.a, dt, ap, K, M, nA, lda * es, M * lda * es, 64, 128, SW))) return rc;
+    const void *bp = B;
+    if (b_mn) {  // B [nB][K][N]
+      int64_t ldb = N;
+      if (((uintptr_t)B & 15) || (N * es) % 16) {
+        ldb = round_up(N, 8);
+        if ((rc = sb.get(dev, st, (size_t)(nB * K * ldb) * es))) return rc;
+        MPC_CUDA(dev, cudaMemcpy2DAsync(sb.ptr, ldb * es, B, N * es, N * es, nB * K, cudaMemcpyDeviceToDevice, st));
+        bp = sb.ptr;
+      }
+      if ((rc = make_map_3d(&maps.b, dt, bp, N, K, nB, ldb * es, K * ldb * es, 64, 64, SW))) return rc;
+      rc = launch<kHalf, true, 256, 4>(dev, maps, p, st);
+    } else {  // B [nB][N][K]
+      int64_t ldb = K;
+      if (((uintptr_t)B & 15) || (K * es) % 16) {
+        ldb = round_up(K, 8);
+        if ((rc = sb.get(dev, st, (size_t)(nB * N * ldb) * es))) return rc;
+        MPC_CUDA(dev, cudaMemcpy2DAsync(sb.ptr, ldb * es, B, K * es, K * es, nB * N, cudaMemcpyDeviceToDevice, st));
+        bp = sb.ptr;
+      }
+      if ((rc = make_map_3d(&maps.b, dt, bp, K, N, nB, ldb * es, N * ldb * es, 64, 256, SW))) return rc;
+      rc = launch<kHalf, false, 256, 4>(dev, maps, p, st);
+    }
+  }
+  if (rc) return rc;
+  if (cdst != Cout)
+    MPC_CUDA(dev, cudaMemcpy2DAsync(Cout, N * eo, cdst, ldc * eo, N * eo, batch * M, cudaMemcpyDeviceToDevice, st));
+  return MPC_OK;
+}
+
+}  // namespace mpc
