@@ -4,13 +4,14 @@
 // (packages/tensor-cpu/src/index.ts:755-774; the reference computes it with gemmNT,
 // packages/tensor-core/src/kernels.ts:299-362, in f64 on the host).
 //
-// One persistent CTA per SM, 6 warps, warp-specialised:
+// One persistent CTA per SM, 10 warps, warp-specialised:
 //   warp 0      TMA producer: A / B tiles into a STAGES-deep shared-memory ring (mbarrier full/empty)
 //   warp 1      MMA issuer: one thread issues tcgen05.mma into a TMEM accumulator and commits
 //               stage releases and accumulator completion to mbarriers; also owns the TMEM allocation
-//   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32*(w%4)..+31),
-//               apply alpha / +bias / exact-erf GELU, convert, stage 32x128-byte swizzled blocks
-//               in shared memory and TMA-store them (bounds clipped by the tensor map)
+//   warps 2..9  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32*(w%4)..+31; two
+//               warps per lane quadrant split the columns), apply alpha / +bias / exact-erf GELU,
+//               convert, stage 32-row x 32-column swizzled blocks in shared memory and TMA-store
+//               them (bounds clipped by the tensor map)
 // Two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1.
 //
 // Operand layouts, all with the 128-byte swizzle:
@@ -22,6 +23,7 @@
 // operand into tf32 hi + lo parts (K-major), and the main loop accumulates lo·hi + hi·lo + hi·hi.
 #include <cstdio>
 
+#include "gelu.cuh"
 #include "mpc_internal.h"
 #include "sm100.cuh"
 
@@ -63,7 +65,9 @@ struct Cfg {
   static constexpr int B_BYTES = BN * 128;
   static constexpr int NOPS = KIND == kHalf ? 1 : 2;
   static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
-  static constexpr int EPI_BYTES = 4 * 2 * 4096;  // 4 warps x 2 buffers x (32 rows x 128 B)
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
+  static constexpr int EPI_BYTES = EPI_WARPS * 4096;  // one 32-row x 128-byte staging block per warp
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
@@ -88,84 +92,74 @@ __device__ __forceinline__ void tile_coords(const Params &p, int tile, int &b, i
 __device__ __forceinline__ void batch_index(const Params &p, int b, int &ia, int &ib) {
   ia = 0;
   ib = 0;
-  for (int d = p.brank - 1; d >= 0; --d) {
-    const int i = b % p.bshape[d];
-    b /= p.bshape[d];
-    ia += i * p.a_bstride[d];
-    ib += i * p.b_bstride[d];
+#pragma unroll
+  for (int d = 3; d >= 0; --d) {  // static indices keep the parameter arrays out of local memory
+    if (d < p.brank) {
+      const int i = b % p.bshape[d];
+      b /= p.bshape[d];
+      ia += i * p.a_bstride[d];
+      ib += i * p.b_bstride[d];
+    }
   }
 }
 
-__device__ __forceinline__ float gelu_erf_f32(float x) {
-  // exact GELU x·Φ(x) = 0.5·x·erfc(-x/√2)  (packages/special/src/index.ts:186-193)
-  return 0.5f * x * erfcf(-x * 0.70710678118654752f);
-}
 
-// One 128-byte-per-row output chunk (32 f32 or 64 half columns) of this warp's 32 rows.
-template <int OUT>
-__device__ __forceinline__ void epilogue_chunk(const Params &p, const CUtensorMap *cmap, uint8_t *buf,
-                                               const uint32_t (&r0)[32], const uint32_t (&r1)[32], int col0,
-                                               int row0, int b, int lane) {
-  constexpr int CPC = OUT == MPC_F32 ? 32 : 64;
-  float f[CPC];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r0[j]);
-  if constexpr (CPC == 64) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) f[32 + j] = __uint_as_float(r1[j]);
-  }
+// alpha, +bias and GELU on one 32-column chunk of this warp's 32 rows (lane = row). The math is
+// written once; only the packing below depends on the output type.
+__device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], int col0, int lane) {
   if (p.alpha != 1.0f) {
 #pragma unroll
-    for (int j = 0; j < CPC; ++j) f[j] *= p.alpha;
+    for (int j = 0; j < 32; ++j) f[j] *= p.alpha;
   }
   if (p.epilogue & MPC_EPI_BIAS) {
+    const int c = col0 + lane;
+    const float bl = c < p.N ? __ldg(p.bias + c) : 0.0f;
 #pragma unroll
-    for (int h = 0; h < CPC / 32; ++h) {
-      const int c = col0 + h * 32 + lane;
-      const float bl = c < p.N ? __ldg(p.bias + c) : 0.0f;
-#pragma unroll
-      for (int j = 0; j < 32; ++j) f[h * 32 + j] += __shfl_sync(0xffffffffu, bl, j);
-    }
+    for (int j = 0; j < 32; ++j) f[j] += __shfl_sync(0xffffffffu, bl, j);
   }
   if (p.epilogue & MPC_EPI_GELU) {
 #pragma unroll
-    for (int j = 0; j < CPC; ++j) f[j] = gelu_erf_f32(f[j]);
+    for (int j = 0; j < 32; ++j) f[j] = gelu_erf_f32(f[j]);
   }
-  // Row `lane` of the 32x128-byte block, 16-byte chunk j stored at chunk (j ^ (lane & 7)):
-  // the 128-byte swizzle the store map expects, and conflict-free for these writes.
-  uint8_t *row = buf + lane * 128;
+}
+
+// Writes row `lane` of a 32-row staging block in the layout the store map's swizzle expects:
+// f32 rows are 128 bytes (16-byte chunk j at chunk j ^ (row & 7), the 128-byte swizzle);
+// f16 / bf16 rows are 64 bytes (chunk j at j ^ ((row >> 1) & 3), the 64-byte swizzle).
+// Both orders are bank-conflict free for these 16-byte stores.
+__device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], int out_dtype, int lane) {
+  if (out_dtype == MPC_F32) {
+    uint8_t *row = buf + lane * 128;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    uint4 v;
-    if constexpr (OUT == MPC_F32) {
-      v = make_uint4(__float_as_uint(f[4 * j]), __float_as_uint(f[4 * j + 1]), __float_as_uint(f[4 * j + 2]),
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) =
+          make_uint4(__float_as_uint(f[4 * j]), __float_as_uint(f[4 * j + 1]), __float_as_uint(f[4 * j + 2]),
                      __float_as_uint(f[4 * j + 3]));
-    } else {
-      uint32_t w[4];
+  } else {
+    uint8_t *row = buf + lane * 64;
+    uint32_t w[16];
+    if (out_dtype == MPC_BF16) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        if constexpr (OUT == MPC_BF16) {
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(f[8 * j + 2 * e], f[8 * j + 2 * e + 1]);
-          w[e] = *reinterpret_cast<uint32_t *>(&h2);
-        } else {
-          __half2 h2 = __floats2half2_rn(f[8 * j + 2 * e], f[8 * j + 2 * e + 1]);
-          w[e] = *reinterpret_cast<uint32_t *>(&h2);
-        }
+      for (int e = 0; e < 16; ++e) {
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+        w[e] = *reinterpret_cast<uint32_t *>(&h2);
       }
-      v = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        __half2 h2 = __floats2half2_rn(f[2 * e], f[2 * e + 1]);
+        w[e] = *reinterpret_cast<uint32_t *>(&h2);
+      }
     }
-    *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) = v;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4 *>(row + ((j ^ ((lane >> 1) & 3)) << 4)) =
+          make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
   }
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0 && row0 < p.M && col0 < p.N) {
-    tma_store_3d(cmap, buf, col0, row0, b);
-  }
-  if (lane == 0) tma_store_commit();
 }
 
 template <int KIND, bool B_MN, int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
+__global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
   using C = Cfg<KIND, B_MN, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -188,7 +182,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], C::EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -323,10 +317,13 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       mbar_wait(drain, 0, &never, p.err, kErrWaitConsumer, p.timeout_ns);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    uint8_t *stg = epi + (warp - 2) * 8192;
-    int local = 0, stores = 0;
+    // ---------------- epilogue (warps 2..9) ----------------
+    const int ew = warp - 2;
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access (hardware rule: warp % 4)
+    constexpr int COLS = BN / 2;  // each of the two warps of a quadrant takes half the columns
+    const int col_base = (ew >> 2) * COLS;
+    uint8_t *buf = epi + ew * 4096;
+    int local = 0;
     for (int tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++local) {
       int b, mt, nt;
       tile_coords(p, tile, b, mt, nt);
@@ -334,32 +331,35 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull, p.timeout_ns)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + col_base;
       const int row0 = mt * C::BM + q * 32;
-      const int cpc = p.out_dtype == MPC_F32 ? 32 : 64;
-      const int nchunks = BN / cpc;
-      for (int c = 0; c < nchunks; ++c) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32(t_row + c * cpc, r0);
-        if (cpc == 64) tmem_ld32(t_row + c * cpc + 32, r1);
-        tmem_ld_wait();
-        if (c == nchunks - 1) {
-          // Accumulator fully read: hand it back to the MMA warp before the math and stores.
+      uint32_t r[32];
+      tmem_ld32(t_row, r);
+#pragma unroll 1
+      for (int c = 0; c < COLS / 32; ++c) {
+        tmem_ld_wait(r);
+        float f[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+        if (c + 1 < COLS / 32) {
+          tmem_ld32(t_row + (c + 1) * 32, r);  // next chunk's load overlaps this chunk's math
+        } else {
+          // This warp's share of the accumulator is in registers: release it to the MMA warp.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
         }
-        uint8_t *buf = stg + (stores & 1) * 4096;
-        if (lane == 0) tma_store_wait_read<1>();  // the store issued from this buffer 2 chunks ago has read it
+        const int col0 = nt * BN + col_base + c * 32;
+        epilogue_math(p, f, col0, lane);
+        if (lane == 0) tma_store_wait_read<0>();  // the previous store has finished reading the block
         __syncwarp();
-        const int col0 = nt * BN + c * cpc;
-        if (p.out_dtype == MPC_F32)
-          epilogue_chunk<MPC_F32>(p, &maps.c, buf, r0, r1, col0, row0, b, lane);
-        else if (p.out_dtype == MPC_BF16)
-          epilogue_chunk<MPC_BF16>(p, &maps.c, buf, r0, r1, col0, row0, b, lane);
-        else
-          epilogue_chunk<MPC_F16>(p, &maps.c, buf, r0, r1, col0, row0, b, lane);
-        ++stores;
+        stage_row(buf, f, p.out_dtype, lane);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if (row0 < p.M && col0 < p.N) tma_store_3d(&maps.c, buf, col0, row0, b);
+          tma_store_commit();
+        }
       }
     }
     if (lane == 0) tma_store_wait_all<0>();
@@ -446,7 +446,7 @@ int launch(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) 
     configured[ord] = true;
   }
   const int grid = p.tiles_total < dev->prop.multiProcessorCount ? p.tiles_total : dev->prop.multiProcessorCount;
-  kern<<<grid, 192, C::SMEM, st>>>(maps, p);
+  kern<<<grid, C::THREADS, C::SMEM, st>>>(maps, p);
   dev->launches++;
   return check_launch(dev, "gemm_kernel");
 }
@@ -545,8 +545,8 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
     if ((rc = sc.get(dev, st, (size_t)(batch * M * ldc) * eo))) return rc;
     cdst = sc.ptr;
   }
-  if ((rc = make_map_3d(&maps.c, tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo,
-                        (uint32_t)(128 / eo), 32, SW)))
+  if ((rc = make_map_3d(&maps.c, tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo, 32, 32,
+                        eo == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
 
   if (tf32) {
