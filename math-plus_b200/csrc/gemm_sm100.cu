@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
       tile_coords(p, tile, b, mt, nt);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull, p.timeout_ns)) break;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull, p.timeout_ns)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + col_base;
       const int row0 = mt * C::BM + q * 32;

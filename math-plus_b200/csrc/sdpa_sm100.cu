@@ -1,7 +1,553 @@
+// Fused scaled-dot-product attention, sm_100a: softmax(scale·Q·Kᵀ + mask)·V without materialising
+// the score matrix. Replaces Backend.sdpa (packages/tensor-cpu/src/index.ts:821-840), whose CPU
+// path builds the full Lq x Lk f64 score panel per head (packages/tensor-core/src/nn-kernels.ts:179-239).
+//
+// Tensor-core path (f16 / bf16, head dim 64 or 128, 16-byte aligned operands):
+//   one CTA per (batch, head, 256 query rows) = two 128-row Q tiles sharing every K/V tile; 10 warps:
+//   warps 0-3 / 4-7  online softmax of Q tile 0 / 1, one thread per query row: tcgen05.ld the S row,
+//                    scale (folded with log2 e), mask, row max, exp2, row sum; P (same type as V) is
+//                    tcgen05.st'd back over the first half of the S columns; the O accumulator is
+//                    rescaled in TMEM only when a row max grows by more than 2^8 (lazy rescale)
+//   warp 8           TMA producer: Q once, then K_j / V_j through a 3-slot shared-memory ring
+//   warp 9           one thread issues tcgen05.mma: S_t = Q_t·K_jᵀ (SS, both K-major) and
+//                    O_t += P_t·V_j (A = P from TMEM, B = V MN-major); owns the TMEM allocation
+//   issue order per KV tile j: QK(1,j), PV(0,j), QK(0,j+1), PV(1,j), so each Q tile's softmax runs
+//   while the tensor core works on the other tile. Causal: KV tiles past a Q tile's diagonal are
+//   skipped, only diagonal tiles are masked element-wise.
+//   TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
+// Generic path (any head dim <= 256, f32 / f16 / bf16, any alignment): one warp per query row on the
+// CUDA cores, online softmax in f32 — the role of backend-webgpu's generic sdpa kernel.
+#include <cfloat>
+
 #include "mpc_internal.h"
+#include "sm100.cuh"
+
 namespace mpc {
-int sdpa_run(mpc_device *, const mpc_sdpa_desc *, const void *, const void *, const void *, const void *, void *,
-             float *, cudaStream_t) {
-  return fail(MPC_ERR_UNSUPPORTED, "mpc_sdpa: not built yet");
+namespace attn {
+
+struct Params {
+  int B, H, Hk, Lq, Lk, D;
+  int rep;       // H / Hk
+  int q_blocks;  // ceil(Lq / 256)
+  int causal;
+  float scale_log2;  // scale * log2(e)
+  int mask_kind;
+  const void *mask;
+  long long ms[4];
+  void *out;
+  float *lse;
+  int dtype;
+  uint32_t idesc_qk, idesc_pv;
+  int *err;
+  unsigned long long timeout_ns;
+};
+
+struct Maps {
+  CUtensorMap q, k, v;
+};
+
+template <int D>
+struct Cfg {
+  static constexpr int NSUB = D / 64;             // 128-byte (64-element) column blocks of a head row
+  static constexpr int TILE = 128 * D * 2;        // bytes of one 128-row Q, K or V tile
+  static constexpr int SUB = 128 * 128;           // bytes of one 128-row x 64-column block
+  static constexpr int SLOTS = 3;
+  static constexpr int SMEM = 1024 + 2 * TILE + SLOTS * TILE + 256;
+  static constexpr int THREADS = 320;
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+__device__ __forceinline__ int last_kv(const Params &p, int q0t) {
+  // Last KV tile any row of the Q tile starting at q0t may see.
+  int last_key = p.Lk - 1;
+  if (p.causal) last_key = min(last_key, min(q0t + 127, p.Lq - 1));
+  return last_key < 0 ? -1 : last_key / 128;
 }
+
+__device__ __forceinline__ float mask_add(const Params &p, int b, int h, int q, int k) {
+  const long long off = b * p.ms[0] + h * p.ms[1] + q * p.ms[2] + k * p.ms[3];
+  if (p.mask_kind == MPC_MASK_BOOL) return static_cast<const uint8_t *>(p.mask)[off] ? 0.0f : -INFINITY;
+  return static_cast<const float *>(p.mask)[off] * 1.4426950408889634f;
+}
+
+template <int D>
+__global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ Maps maps, const Params p) {
+  using C = Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sq = smem;                 // Q tile 0, Q tile 1
+  uint8_t *skv = smem + 2 * C::TILE;  // ring of SLOTS K/V tiles
+  uint64_t *bars = reinterpret_cast<uint64_t *>(skv + C::SLOTS * C::TILE);
+  uint64_t *q_full = bars;
+  uint64_t *kv_full = bars + 1;
+  uint64_t *kv_empty = kv_full + C::SLOTS;
+  uint64_t *s_ready = kv_empty + C::SLOTS;  // [2]
+  uint64_t *p_ready = s_ready + 2;          // [2]
+  uint64_t *o_ready = p_ready + 2;          // [2]
+  uint64_t *drain = o_ready + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int BH = p.B * p.H;
+  const int qb = p.q_blocks - 1 - (int)(blockIdx.x / BH);  // heaviest (causal) blocks first
+  const int bh = blockIdx.x % BH;
+  const int b = bh / p.H, h = bh % p.H;
+  const int kvh = b * p.Hk + h / p.rep;
+  const int q0 = qb * 256;
+  const bool valid1 = q0 + 128 < p.Lq;
+  const int last0 = last_kv(p, q0);
+  const int last1 = valid1 ? last_kv(p, q0 + 128) : -1;
+  const int n_kv = max(last0, last1) + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::SLOTS; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&s_ready[t], 1);
+      mbar_init(&p_ready[t], 4);
+      mbar_init(&o_ready[t], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_desc(&maps.q);
+      tma_prefetch_desc(&maps.k);
+      tma_prefetch_desc(&maps.v);
+      const int nq = valid1 ? 2 : 1;
+      mbar_expect_tx(q_full, nq * C::TILE);
+      for (int t = 0; t < nq; ++t)
+        for (int s = 0; s < C::NSUB; ++s)
+          tma_load_3d(&maps.q, q_full, sq + t * C::TILE + s * C::SUB, s * 64, q0 + 128 * t, bh);
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; ok && i < 2 * n_kv; ++i) {
+        const int slot = i % C::SLOTS;
+        const uint32_t ph = (i / C::SLOTS) & 1;
+        if (!mbar_wait(&kv_empty[slot], ph ^ 1, abort_flag, p.err, kErrWaitProducer, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        const CUtensorMap *map = (i & 1) ? &maps.v : &maps.k;
+        mbar_expect_tx(&kv_full[slot], C::TILE);
+        for (int s = 0; s < C::NSUB; ++s)
+          tma_load_3d(map, &kv_full[slot], skv + slot * C::TILE + s * C::SUB, s * 64, (i >> 1) * 128, kvh);
+        ++issued;
+      }
+      if (!ok) {  // let the copies in flight land before shared memory is released
+        volatile int never = 0;
+        mbar_wait(q_full, 0, &never, p.err, kErrWaitProducer, p.timeout_ns);
+        const int n = issued < C::SLOTS ? issued : C::SLOTS;
+        for (int i = issued - n; i < issued; ++i)
+          mbar_wait(&kv_full[i % C::SLOTS], (i / C::SLOTS) & 1, &never, p.err, kErrWaitProducer, p.timeout_ns);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_kv > 0) {
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns);
+      const uint32_t q_addr = smem_u32(sq);
+      auto qk = [&](int t, int slot) {
+        const uint32_t a0 = q_addr + t * C::TILE, b0 = smem_u32(skv + slot * C::TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * C::SUB + (kk & 3) * 32;
+          mma_f16_ss(tmem + t * 128, make_sdesc(a0 + off, 16, 1024), make_sdesc(b0 + off, 16, 1024), p.idesc_qk,
+                     kk ? 1u : 0u);
+        }
+      };
+      auto pv = [&](int t, int slot, bool first) {
+        const uint32_t v0 = smem_u32(skv + slot * C::TILE);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per MMA; P packs 2 keys per TMEM column
+          mma_f16_ts(tmem + 256 + t * D, tmem + t * 128 + kk * 8, make_sdesc(v0 + kk * 2048, C::SUB, 1024),
+                     p.idesc_pv, (first && kk == 0) ? 0u : 1u);
+      };
+      auto need = [&](int t, int j) { return j <= (t ? last1 : last0); };
+      // K_j is ring item 2j, V_j item 2j+1.
+      auto wait_item = [&](int i) {
+        return mbar_wait(&kv_full[i % C::SLOTS], (i / C::SLOTS) & 1, abort_flag, p.err, kErrWaitConsumer,
+                         p.timeout_ns);
+      };
+      if (ok) ok = wait_item(0);
+      if (ok) {
+        tc_fence_after();
+        if (need(0, 0)) {
+          qk(0, 0);
+          tc_commit(&s_ready[0]);
+        }
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int sk = (2 * j) % C::SLOTS, sv = (2 * j + 1) % C::SLOTS;
+        if (need(1, j)) {
+          qk(1, sk);
+          tc_commit(&s_ready[1]);
+        }
+        tc_commit(&kv_empty[sk]);  // K_j is consumed once both QK products have run
+        if (!(ok = wait_item(2 * j + 1))) break;
+        tc_fence_after();
+        if (need(0, j)) {
+          if (!(ok = mbar_wait(&p_ready[0], j & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
+          tc_fence_after();
+          pv(0, sv, j == 0);
+          tc_commit(&o_ready[0]);
+        }
+        if (j + 1 < n_kv) {
+          if (!(ok = wait_item(2 * (j + 1)))) break;
+          tc_fence_after();
+          if (need(0, j + 1)) {
+            qk(0, (2 * (j + 1)) % C::SLOTS);
+            tc_commit(&s_ready[0]);
+          }
+        }
+        if (need(1, j)) {
+          if (!(ok = mbar_wait(&p_ready[1], j & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
+          tc_fence_after();
+          pv(1, sv, j == 0);
+          tc_commit(&o_ready[1]);
+        }
+        tc_commit(&kv_empty[sv]);
+      }
+      tc_commit(drain);
+      volatile int never = 0;
+      mbar_wait(drain, 0, &never, p.err, kErrWaitConsumer, p.timeout_ns);
+    }
+  } else {
+    // ---------------- softmax + correction + output (warps 0-7) ----------------
+    const int t = warp >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int q = q0 + 128 * t + row;
+    const int last = t ? last1 : last0;
+    const bool tile_valid = t == 0 || valid1;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + t * 128;
+    const uint32_t o_addr = tmem + lane_base + 256 + t * D;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    if (tile_valid) {
+      for (int j = 0; j <= last; ++j) {
+        if (!(ok = mbar_wait_warp(&s_ready[t], j & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
+        tc_fence_after();
+        const int k0 = j * 128;
+        const bool edge = k0 + 127 >= p.Lk || (p.causal && k0 + 127 > q0 + 128 * t);
+        const bool masked = p.mask_kind != MPC_MASK_NONE && q < p.Lq;
+        // Scaled, masked scores of one 32-key chunk (recomputed in both passes).
+        auto chunk = [&](int c, float (&v)[32]) {
+          uint32_t r[32];
+          tmem_ld32(s_addr + c * 32, r);
+          tmem_ld_wait(r);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]) * p.scale_log2;
+          if (edge) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int k = k0 + c * 32 + e;
+              if (k >= p.Lk || (p.causal && k > q)) v[e] = -INFINITY;
+            }
+          }
+          if (masked) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (k0 + c * 32 + e < p.Lk) v[e] += mask_add(p, b, h, q, k0 + c * 32 + e);
+          }
+        };
+        // pass 1: row max of the tile
+        float mt = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          chunk(c, v);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mt = fmaxf(mt, v[e]);
+        }
+        const float m_new = fmaxf(m, mt);
+        const bool grow = m_new > m + 8.0f;  // lazy rescale: P stays below 2^8 otherwise
+        if (__any_sync(0xffffffffu, grow)) {
+          const float factor = (m == -INFINITY) ? 0.0f : exp2f(m - m_new);
+          if (j > 0) {
+            if (!(ok = mbar_wait_warp(&o_ready[t], (j - 1) & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns)))
+              break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < D / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld32(o_addr + c * 32, r);
+              tmem_ld_wait(r);
+#pragma unroll
+              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * factor);
+              tmem_st32(o_addr + c * 32, r);
+            }
+            tmem_st_wait();
+          }
+          l *= factor;
+          m = m_new;
+        }
+        const float m_use = m == -INFINITY ? 0.0f : m;
+        // pass 2: P = exp2(s - m) packed two keys per column (key 2e in the low half of column e),
+        // written over S columns [16c, 16c+16), which chunk c-1 or earlier has already consumed.
+        float rs = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          chunk(c, v);
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const float a = exp2f(v[2 * e] - m_use), bb = exp2f(v[2 * e + 1] - m_use);
+            rs += a + bb;
+            if (p.dtype == MPC_BF16) {
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(a, bb);
+              w[e] = *reinterpret_cast<uint32_t *>(&v2);
+            } else {
+              __half2 v2 = __floats2half2_rn(a, bb);
+              w[e] = *reinterpret_cast<uint32_t *>(&v2);
+            }
+          }
+          tmem_st16(s_addr + c * 16, w);
+        }
+        l += rs;
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_ready[t]);
+      }
+      // ---- output: O / l, rows below Lq ----
+      if (ok && last >= 0) ok = mbar_wait_warp(&o_ready[t], last & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns);
+      tc_fence_after();
+      if (ok && last >= 0) {
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        const size_t orow = ((size_t)bh * p.Lq + (size_t)q) * D;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(o_addr + c * 32, r);
+          tmem_ld_wait(r);
+          if (q < p.Lq) {
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              const float a = __uint_as_float(r[2 * e]) * inv, bb = __uint_as_float(r[2 * e + 1]) * inv;
+              if (p.dtype == MPC_BF16) {
+                __nv_bfloat162 v2 = __floats2bfloat162_rn(a, bb);
+                w[e] = *reinterpret_cast<uint32_t *>(&v2);
+              } else {
+                __half2 v2 = __floats2half2_rn(a, bb);
+                w[e] = *reinterpret_cast<uint32_t *>(&v2);
+              }
+            }
+            uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.out) + orow + c * 32);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+          }
+        }
+        if (p.lse && q < p.Lq)
+          p.lse[(size_t)bh * p.Lq + q] = l > 0.0f ? (m * 0.6931471805599453f + logf(l)) : -INFINITY;
+      } else if (last < 0 && q < p.Lq && tile_valid) {
+        // No key is visible to this tile at all (Lk == 0): the fully-masked-row convention, zeros.
+        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.out) + ((size_t)bh * p.Lq + q) * D);
+        for (int e = 0; e < D / 8; ++e) dst[e] = make_uint4(0, 0, 0, 0);
+        if (p.lse) p.lse[(size_t)bh * p.Lq + q] = -INFINITY;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Generic CUDA-core path: one warp per query row, keys in chunks of 32 (lane = key), f32 math.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float ld(const void *p, int dt, size_t i) {
+  if (dt == MPC_F32) return static_cast<const float *>(p)[i];
+  if (dt == MPC_BF16) return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+  return __half2float(static_cast<const __half *>(p)[i]);
+}
+__device__ __forceinline__ void st(void *p, int dt, size_t i, float v) {
+  if (dt == MPC_F32)
+    static_cast<float *>(p)[i] = v;
+  else if (dt == MPC_BF16)
+    static_cast<__nv_bfloat16 *>(p)[i] = __float2bfloat16_rn(v);
+  else
+    static_cast<__half *>(p)[i] = __float2half_rn(v);
+}
+
+struct GenericParams {
+  int B, H, Hk, Lq, Lk, D, Dv, rep, causal, dtype, mask_kind;
+  float scale;
+  const void *q, *k, *v, *mask;
+  long long ms[4];
+  void *out;
+  float *lse;
+};
+
+__global__ void attn_generic_kernel(const GenericParams p) {
+  __shared__ float qs[8][256];
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long row_id = (long long)blockIdx.x * 8 + w;  // over B*H*Lq
+  const long long rows = (long long)p.B * p.H * p.Lq;
+  if (row_id >= rows) return;
+  const int q = (int)(row_id % p.Lq);
+  const int bh = (int)(row_id / p.Lq);
+  const int b = bh / p.H, h = bh % p.H;
+  const int kvh = b * p.Hk + h / p.rep;
+  for (int d = lane; d < p.D; d += 32) qs[w][d] = ld(p.q, p.dtype, (size_t)row_id * p.D + d);
+  __syncwarp();
+  float m = -INFINITY, l = 0.0f;
+  float o[8];  // dims lane, lane+32, ..., Dv <= 256
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+  const int k_end = p.causal ? min(p.Lk, q + 1) : p.Lk;
+  for (int k0 = 0; k0 < k_end; k0 += 32) {
+    const int k = k0 + lane;
+    float s = -INFINITY;
+    if (k < k_end) {
+      float acc = 0.0f;
+      const size_t kb = ((size_t)kvh * p.Lk + k) * p.D;
+      for (int d = 0; d < p.D; ++d) acc = fmaf(qs[w][d], ld(p.k, p.dtype, kb + d), acc);
+      s = acc * p.scale;
+      if (p.mask_kind != MPC_MASK_NONE) {
+        const long long off = b * p.ms[0] + h * p.ms[1] + q * p.ms[2] + k * p.ms[3];
+        if (p.mask_kind == MPC_MASK_BOOL)
+          s = static_cast<const uint8_t *>(p.mask)[off] ? s : -INFINITY;
+        else
+          s += static_cast<const float *>(p.mask)[off];
+      }
+    }
+    float mt = s;
+#pragma unroll
+    for (int o2 = 16; o2; o2 >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o2));
+    const float m_new = fmaxf(m, mt);
+    if (m_new == -INFINITY) continue;  // nothing visible yet
+    const float factor = m == -INFINITY ? 0.0f : expf(m - m_new);
+    const float pk = s == -INFINITY ? 0.0f : expf(s - m_new);
+    float ps = pk;
+#pragma unroll
+    for (int o2 = 16; o2; o2 >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o2);
+    l = l * factor + ps;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] *= factor;
+    const int nk = min(32, k_end - k0);
+    for (int jj = 0; jj < nk; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, pk, jj);
+      if (pj == 0.0f) continue;  // masked keys contribute nothing (even a non-finite V row)
+      const size_t vb = ((size_t)kvh * p.Lk + k0 + jj) * p.Dv;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int d = lane + 32 * i;
+        if (d < p.Dv) o[i] = fmaf(pj, ld(p.v, p.dtype, vb + d), o[i]);
+      }
+    }
+    m = m_new;
+  }
+  const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = lane + 32 * i;
+    if (d < p.Dv) st(p.out, p.dtype, (size_t)row_id * p.Dv + d, o[i] * inv);
+  }
+  if (p.lse && lane == 0) p.lse[row_id] = l > 0.0f ? m + logf(l) : -INFINITY;
+}
+
+template <int D>
+int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
+  using C = Cfg<D>;
+  static bool configured[64] = {};
+  const int ord = dev->ordinal & 63;
+  if (!configured[ord]) {
+    MPC_CUDA(dev, cudaFuncSetAttribute(attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    configured[ord] = true;
+  }
+  const long long grid = (long long)p.q_blocks * p.B * p.H;
+  attn_kernel<D><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(maps, p);
+  dev->launches++;
+  return check_launch(dev, "attn_kernel");
+}
+
+}  // namespace attn
+
+int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void *K, const void *V, const void *mask,
+             void *O, float *LSE, cudaStream_t st) {
+  using namespace attn;
+  if (d->b < 0 || d->h <= 0 || d->hk <= 0 || d->lq < 0 || d->lk < 0 || d->d <= 0 || d->dv <= 0)
+    return fail(MPC_ERR_INVALID, "mpc_sdpa: bad extents b=%lld h=%lld hk=%lld lq=%lld lk=%lld d=%lld dv=%lld",
+                (long long)d->b, (long long)d->h, (long long)d->hk, (long long)d->lq, (long long)d->lk,
+                (long long)d->d, (long long)d->dv);
+  if (d->h % d->hk) return fail(MPC_ERR_INVALID, "mpc_sdpa: H=%lld is not a multiple of Hk=%lld", (long long)d->h,
+                                (long long)d->hk);
+  if (d->dtype != MPC_F32 && d->dtype != MPC_F16 && d->dtype != MPC_BF16)
+    return fail(MPC_ERR_INVALID, "mpc_sdpa: dtype %d", d->dtype);
+  if (d->mask_kind < MPC_MASK_NONE || d->mask_kind > MPC_MASK_ADD || (d->mask_kind && !mask))
+    return fail(MPC_ERR_INVALID, "mpc_sdpa: mask_kind %d with mask %p", d->mask_kind, mask);
+  if (d->b == 0 || d->lq == 0) return MPC_OK;
+  if (!Q || !K || !V || !O) return fail(MPC_ERR_INVALID, "mpc_sdpa: null operand");
+  if (d->b * d->h > (1 << 30) || d->lq > (1 << 30) || d->lk > (1 << 30))
+    return fail(MPC_ERR_UNSUPPORTED, "mpc_sdpa: extents above 2^30");
+  const bool aligned = !((uintptr_t)Q & 15) && !((uintptr_t)K & 15) && !((uintptr_t)V & 15) && !((uintptr_t)O & 15);
+  const bool tc = d->dtype != MPC_F32 && d->d == d->dv && (d->d == 64 || d->d == 128) && aligned && d->lk > 0;
+  if (!tc) {
+    if (d->d > 256 || d->dv > 256) return fail(MPC_ERR_UNSUPPORTED, "mpc_sdpa: head dim above 256");
+    GenericParams g{};
+    g.B = (int)d->b, g.H = (int)d->h, g.Hk = (int)d->hk, g.Lq = (int)d->lq, g.Lk = (int)d->lk, g.D = (int)d->d;
+    g.Dv = (int)d->dv, g.rep = (int)(d->h / d->hk), g.causal = d->causal ? 1 : 0, g.dtype = d->dtype;
+    g.mask_kind = d->mask_kind, g.scale = d->scale, g.q = Q, g.k = K, g.v = V, g.mask = mask, g.out = O, g.lse = LSE;
+    for (int i = 0; i < 4; ++i) g.ms[i] = d->mask_strides[i];
+    const long long rows = d->b * d->h * d->lq;
+    attn_generic_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(g);
+    dev->launches++;
+    return check_launch(dev, "attn_generic_kernel");
+  }
+  Params p{};
+  p.B = (int)d->b, p.H = (int)d->h, p.Hk = (int)d->hk, p.Lq = (int)d->lq, p.Lk = (int)d->lk, p.D = (int)d->d;
+  p.rep = p.H / p.Hk;
+  p.q_blocks = (p.Lq + 255) / 256;
+  p.causal = d->causal ? 1 : 0;
+  p.scale_log2 = d->scale * 1.4426950408889634f;
+  p.mask_kind = d->mask_kind;
+  p.mask = mask;
+  for (int i = 0; i < 4; ++i) p.ms[i] = d->mask_strides[i];
+  p.out = O;
+  p.lse = LSE;
+  p.dtype = d->dtype;
+  const uint32_t fmt = d->dtype == MPC_BF16 ? kFmtBF16 : kFmtF16;
+  p.idesc_qk = make_idesc(fmt, false, 128, 128);
+  p.idesc_pv = make_idesc(fmt, true, 128, p.D);
+  p.err = dev->d_err;
+  p.timeout_ns = dev->timeout_ns;
+  Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  const CUtensorMapDataType dt = d->dtype == MPC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t rowb = (uint64_t)p.D * 2;
+  int rc;
+  if ((rc = make_map_3d(&maps.q, dt, Q, p.D, p.Lq, (uint64_t)p.B * p.H, rowb, rowb * p.Lq, 64, 128,
+                        CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_map_3d(&maps.k, dt, K, p.D, p.Lk, (uint64_t)p.B * p.Hk, rowb, rowb * p.Lk, 64, 128,
+                        CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_map_3d(&maps.v, dt, V, p.D, p.Lk, (uint64_t)p.B * p.Hk, rowb, rowb * p.Lk, 64, 128,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  return p.D == 128 ? launch_tc<128>(dev, maps, p, st) : launch_tc<64>(dev, maps, p, st);
+}
+
 }  // namespace mpc
