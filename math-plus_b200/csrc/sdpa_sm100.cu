@@ -3,14 +3,15 @@
 // path builds the full Lq x Lk f64 score panel per head (packages/tensor-core/src/nn-kernels.ts:179-239).
 //
 // Tensor-core path (f16 / bf16, head dim 64 or 128, 16-byte aligned operands):
-//   one CTA per (batch, head, 256 query rows) = two 128-row Q tiles sharing every K/V tile; 10 warps:
+//   one CTA per (batch, head, 256 query rows) = two 128-row Q tiles sharing every K/V tile; 12 warps:
 //   warps 0-3 / 4-7  online softmax of Q tile 0 / 1, one thread per query row: tcgen05.ld the S row,
 //                    scale (folded with log2 e), mask, row max, exp2, row sum; P (same type as V) is
 //                    tcgen05.st'd back over the first half of the S columns; the O accumulator is
 //                    rescaled in TMEM only when a row max grows by more than 2^8 (lazy rescale)
-//   warp 8           TMA producer: Q once, then K_j / V_j through a 3-slot shared-memory ring
+//   warp 8           TMA producer: Q once, then K_j / V_j through a 5-slot shared-memory ring
 //   warp 9           one thread issues tcgen05.mma: S_t = Q_t·K_jᵀ (SS, both K-major) and
 //                    O_t += P_t·V_j (A = P from TMEM, B = V MN-major); owns the TMEM allocation
+//   warps 10-11      idle (they complete the load / MMA warpgroup for register reconfiguration)
 //   issue order per KV tile j: QK(1,j), PV(0,j), QK(0,j+1), PV(1,j), so each Q tile's softmax runs
 //   while the tensor core works on the other tile. Causal: KV tiles past a Q tile's diagonal are
 //   skipped, only diagonal tiles are masked element-wise.
@@ -51,9 +52,9 @@ struct Cfg {
   static constexpr int NSUB = D / 64;             // 128-byte (64-element) column blocks of a head row
   static constexpr int TILE = 128 * D * 2;        // bytes of one 128-row Q, K or V tile
   static constexpr int SUB = 128 * 128;           // bytes of one 128-row x 64-column block
-  static constexpr int SLOTS = 3;
+  static constexpr int SLOTS = D == 128 ? 5 : 8;  // K/V ring depth: 2.5 (D=128) or 4 KV tiles ahead
   static constexpr int SMEM = 1024 + 2 * TILE + SLOTS * TILE + 256;
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 384;  // 3 warpgroups: softmax 0, softmax 1, load / MMA
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
@@ -71,7 +72,7 @@ __device__ __forceinline__ float mask_add(const Params &p, int b, int h, int q, 
 }
 
 template <int D>
-__global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ Maps maps, const Params p) {
+__global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Maps maps, const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -89,9 +90,10 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ Ma
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int BH = p.B * p.H;
-  const int qb = p.q_blocks - 1 - (int)(blockIdx.x / BH);  // heaviest (causal) blocks first
-  const int bh = blockIdx.x % BH;
+  // Head-major order: the CTAs running together share a few heads' K/V in L2; within a head the
+  // heaviest (causal) query blocks go first, so the grid ends on light blocks.
+  const int bh = (int)(blockIdx.x / p.q_blocks);
+  const int qb = p.q_blocks - 1 - (int)(blockIdx.x % p.q_blocks);
   const int b = bh / p.H, h = bh % p.H;
   const int kvh = b * p.Hk + h / p.rep;
   const int q0 = qb * 256;
@@ -124,7 +126,14 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ Ma
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 8) {
+  // Register reconfiguration (at the head of each role's branch): the load / MMA warpgroup
+  // gives registers to the two softmax warpgroups, which keep a whole 128-key score row in
+  // registers. Launched at 168 per thread (the host checks):
+  // 2 x 128 x 224 + 128 x 56 = 64512 = 384 x 168.
+  if (warp >= 10) {
+    reg_dealloc<56>();  // the warpgroup's two spare warps only wait for the end
+  } else if (warp == 8) {
+    reg_dealloc<56>();
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_desc(&maps.q);
@@ -160,6 +169,7 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ Ma
     }
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
+    reg_dealloc<56>();
     if (lane == 0 && n_kv > 0) {
       bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns);
       const uint32_t q_addr = smem_u32(sq);
@@ -230,6 +240,7 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ Ma
     }
   } else {
     // ---------------- softmax + correction + output (warps 0-7) ----------------
+    reg_alloc<224>();
     const int t = warp >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
@@ -248,35 +259,43 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ Ma
         const int k0 = j * 128;
         const bool edge = k0 + 127 >= p.Lk || (p.causal && k0 + 127 > q0 + 128 * t);
         const bool masked = p.mask_kind != MPC_MASK_NONE && q < p.Lq;
-        // Scaled, masked scores of one 32-key chunk (recomputed in both passes).
-        auto chunk = [&](int c, float (&v)[32]) {
-          uint32_t r[32];
-          tmem_ld32(s_addr + c * 32, r);
-          tmem_ld_wait(r);
+        // The whole 128-key row in registers: four loads in flight, one wait.
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(s_addr, r0);
+        tmem_ld32(s_addr + 32, r1);
+        tmem_ld32(s_addr + 64, r2);
+        tmem_ld32(s_addr + 96, r3);
+        tmem_ld_wait(r0);
+        tmem_ld_wait(r1);
+        tmem_ld_wait(r2);
+        tmem_ld_wait(r3);
+        float v[128];
 #pragma unroll
-          for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]) * p.scale_log2;
-          if (edge) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int k = k0 + c * 32 + e;
-              if (k >= p.Lk || (p.causal && k > q)) v[e] = -INFINITY;
-            }
-          }
-          if (masked) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              if (k0 + c * 32 + e < p.Lk) v[e] += mask_add(p, b, h, q, k0 + c * 32 + e);
-          }
-        };
-        // pass 1: row max of the tile
-        float mt = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          chunk(c, v);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) mt = fmaxf(mt, v[e]);
+        for (int e = 0; e < 32; ++e) {
+          v[e] = __uint_as_float(r0[e]);
+          v[32 + e] = __uint_as_float(r1[e]);
+          v[64 + e] = __uint_as_float(r2[e]);
+          v[96 + e] = __uint_as_float(r3[e]);
         }
+        // Scores stay unscaled (scale > 0 commutes with the max) unless a mask must be added.
+        float scl = p.scale_log2;
+        if (edge) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) {
+            const int k = k0 + c;
+            if (k >= p.Lk || (p.causal && k > q)) v[c] = -INFINITY;
+          }
+        }
+        if (masked || scl < 0.0f) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            v[c] = fmaf(v[c], scl, (masked && k0 + c < p.Lk) ? mask_add(p, b, h, q, k0 + c) : 0.0f);
+          scl = 1.0f;
+        }
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 128; ++c) mx[c & 3] = fmaxf(mx[c & 3], v[c]);
+        const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scl;
         const float m_new = fmaxf(m, mt);
         const bool grow = m_new > m + 8.0f;  // lazy rescale: P stays below 2^8 otherwise
         if (__any_sync(0xffffffffu, grow)) {
@@ -299,30 +318,33 @@ __global__ void __launch_bounds__(320, 1) attn_kernel(const __grid_constant__ Ma
           l *= factor;
           m = m_new;
         }
-        const float m_use = m == -INFINITY ? 0.0f : m;
-        // pass 2: P = exp2(s - m) packed two keys per column (key 2e in the low half of column e),
-        // written over S columns [16c, 16c+16), which chunk c-1 or earlier has already consumed.
-        float rs = 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          chunk(c, v);
-          uint32_t w[16];
+        const float neg_m = m == -INFINITY ? 0.0f : -m;
+        // P = exp2(s·scale - m), packed two keys per TMEM column (key 2e in the low half of column e),
+        // over the first 64 S columns (the row is already in registers). The exponentials run two
+        // at a time on the f16x2 path of the special-function unit; the argument's f16 rounding
+        // perturbs P by at most 2^-11·ln2·|x| relative (<= 0.6% for the P < 2^-8 that |x| > 8
+        // gives). The row sum stays f32.
+        float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        uint32_t w0[32], w1[32];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float a = exp2f(v[2 * e] - m_use), bb = exp2f(v[2 * e + 1] - m_use);
-            rs += a + bb;
-            if (p.dtype == MPC_BF16) {
-              __nv_bfloat162 v2 = __floats2bfloat162_rn(a, bb);
-              w[e] = *reinterpret_cast<uint32_t *>(&v2);
-            } else {
-              __half2 v2 = __floats2half2_rn(a, bb);
-              w[e] = *reinterpret_cast<uint32_t *>(&v2);
-            }
+        for (int e = 0; e < 64; ++e) {
+          const __half2 x2 = __floats2half2_rn(fmaf(v[2 * e], scl, neg_m), fmaf(v[2 * e + 1], scl, neg_m));
+          const uint32_t e2 = ex2_f16x2(*reinterpret_cast<const uint32_t *>(&x2));
+          const float2 pf = __half22float2(*reinterpret_cast<const __half2 *>(&e2));
+          rs[e & 3] += pf.x + pf.y;
+          uint32_t packed = e2;
+          if (p.dtype == MPC_BF16) {
+            __nv_bfloat162 v2 = __floats2bfloat162_rn(pf.x, pf.y);
+            packed = *reinterpret_cast<uint32_t *>(&v2);
           }
-          tmem_st16(s_addr + c * 16, w);
+          if (e < 32)
+            w0[e] = packed;
+          else
+            w1[e - 32] = packed;
         }
-        l += rs;
+        tmem_st32(s_addr, w0);
+        tmem_st32(s_addr + 32, w1);
+        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -477,6 +499,12 @@ int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t s
   const int ord = dev->ordinal & 63;
   if (!configured[ord]) {
     MPC_CUDA(dev, cudaFuncSetAttribute(attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    cudaFuncAttributes fa;
+    MPC_CUDA(dev, cudaFuncGetAttributes(&fa, attn_kernel<D>));
+    // The register split inside the kernel is sized for a 168-register launch; refuse anything else
+    // rather than launch a split whose increase could never be granted.
+    if (fa.numRegs != 168)
+      return fail(MPC_ERR_UNSUPPORTED, "attn_kernel built with %d registers per thread (expected 168)", fa.numRegs);
     configured[ord] = true;
   }
   const long long grid = (long long)p.q_blocks * p.B * p.H;
