@@ -135,6 +135,19 @@ typedef struct {
 int mpc_gemm(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B, void *C,
              const float *bias, mpc_stream s);
 
+/* Allocation-free variant of the f32 (3xTF32) path of mpc_gemm. It has no counterpart in the
+ * reference: it exists for callers that cannot allocate device memory (code running during
+ * CUDA-graph capture, runtimes that own every device byte or hand out a fixed budget). Its
+ * scratch (the tf32 hi/lo planes, and a padded copy of C when C's rows are not 16-byte aligned)
+ * lives in one static device array of 32 MiB that every GPU loading the library holds until
+ * exit; requests needing more return MPC_ERR_INVALID. It uses the calling thread's current
+ * device and the given stream (NULL = the legacy default stream) and needs no mpc_device. The
+ * first call on a device resolves the array's address (cudaGetSymbolAddress): make it before any
+ * stream capture. All calls share the array: calls that overlap on the GPU race. desc must say
+ * f32 in and out; everything else is as for mpc_gemm. */
+int mpc_gemm_f32_noalloc(const mpc_gemm_desc *desc, const float *A, const float *B, float *C,
+                         const float *bias, mpc_stream s);
+
 /* ---- fused scaled-dot-product attention ----------------------------------------------------
  * softmax(scale * Q·Kᵀ + mask) · V over Q [B,H,Lq,D], K [B,Hk,Lk,D], V [B,Hk,Lk,Dv] into
  * O [B,H,Lq,Dv] (all contiguous), H a multiple of Hk (grouped-query heads share K/V).

@@ -90,6 +90,7 @@ SIGNATURES = {
     "mpc_sync": [_dev],
     "mpc_launch_count": [_dev, C.POINTER(_u64)],
     "mpc_gemm": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
+    "mpc_gemm_f32_noalloc": [C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
     "mpc_sdpa": [_dev, C.POINTER(SdpaDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "mpc_softmax": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, _vp],
     "mpc_gelu": [_dev, _vp, _i32, _vp, _i32, _i64, _vp],
