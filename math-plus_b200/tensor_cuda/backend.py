@@ -1,0 +1,434 @@
+"""``CudaBackend``: the ``@johnhenry/tensor-backend`` ``Backend`` contract over libmathplus_cuda.so.
+
+Mirrors the method set of tensor-cpu's ``CpuBackendImpl`` (packages/tensor-cpu/src/index.ts:200-861)
+for the GEMM / attention path: transfers (``fromHost`` / ``read``, async), lifetime (``dispose``,
+``scope``, ``flush``, ``destroy``), ``reshape``, ``cast``, ``add``, ``gelu``, ``softmax``,
+``matmul``, ``linear``, ``sdpa``, ``layerNorm``, ``embedding``.
+
+Lazy inside, eager-observable (RFC 0001 §12 Q1, as the MLX and WebGPU backends): ``matmul`` and
+``linear`` return a handle whose GEMM has not run yet; an ``add`` of a bias row and a ``gelu``
+applied to that handle fold into the GEMM's epilogue, so ``x.matmul(w).add(b).gelu()`` is one
+kernel. Anything that reads the handle (another op, ``read``, ``flush``) runs it. Shape and dtype
+errors are raised at the call site.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, replace
+
+import numpy as np
+
+from . import _ffi as F
+from . import plan as P
+from .runtime import Device, DeviceBuffer, gemm_desc, sdpa_desc
+
+FLOAT = ("f32", "f16", "bf16")
+STORAGE = {"f32": np.float32, "f16": np.float16, "bf16": np.uint16, "i32": np.int32, "bool": np.uint8}
+
+
+@dataclass
+class HostTensor:
+    """tensor-backend's ``HostTensor``: dtype, shape and flat data (bf16 as raw uint16 bits)."""
+    dtype: str
+    shape: tuple
+    data: np.ndarray
+
+
+def host(dtype: str, shape, data) -> HostTensor:
+    """tensor-backend's ``host()`` helper: values are converted to the dtype's storage."""
+    shape = tuple(int(s) for s in shape)
+    if dtype == "bf16":
+        arr = np.asarray(data)
+        if arr.dtype != np.uint16:
+            x = np.ascontiguousarray(arr, np.float32).view(np.uint32).astype(np.uint64)
+            arr = ((x + 0x7FFF + ((x >> 16) & 1)) >> 16).astype(np.uint16)
+    elif dtype == "bool":
+        arr = (np.asarray(data) != 0).astype(np.uint8)
+    else:
+        arr = np.asarray(data, dtype=STORAGE[dtype])
+    return HostTensor(dtype, shape, np.ascontiguousarray(arr).reshape(-1))
+
+
+@dataclass
+class _PendingGemm:
+    """A GEMM not yet run. It holds references to its operands' buffers, so disposing the operand
+    arrays does not free memory the GEMM will still read."""
+    a: DeviceBuffer
+    b: DeviceBuffer
+    dtype_in: str
+    b_layout: int
+    m: int
+    n: int
+    k: int
+    batch_shape: tuple
+    a_strides: tuple
+    b_strides: tuple
+    bias: DeviceBuffer | None = None
+    bias_dtype: str = "f32"
+    epilogue: int = 0
+
+    def retain(self) -> "_PendingGemm":
+        for b in (self.a, self.b, self.bias):
+            if b is not None:
+                b.retain()
+        return self
+
+    def release(self) -> None:
+        for b in (self.a, self.b, self.bias):
+            if b is not None:
+                b.release()
+
+
+class CudaTensor:
+    """A backend handle: shape, dtype and device memory (or a GEMM that has not run yet)."""
+
+    def __init__(self, backend: "CudaBackend", shape, dtype: str, buf: DeviceBuffer | None = None,
+                 pending: _PendingGemm | None = None):
+        self.backend = backend
+        self.shape = tuple(int(s) for s in shape)
+        self.dtype = dtype
+        self._buf = buf
+        self._pending = pending
+        self.disposed = False
+
+    @property
+    def size(self) -> int:
+        n = 1
+        for s in self.shape:
+            n *= s
+        return n
+
+    @property
+    def nbytes(self) -> int:
+        return self.size * F.DTYPE_BYTES[F.DTYPE_CODES[self.dtype]]
+
+    @property
+    def ptr(self) -> int:
+        """Device address; runs a pending GEMM first."""
+        if self.disposed:
+            raise RuntimeError("tensor-cuda: tensor used after dispose")
+        if self._pending is not None:
+            self.backend._run_gemm(self)
+        return self._buf.ptr
+
+    def _release(self) -> None:
+        if self.disposed:
+            return
+        if self._buf is not None:
+            self._buf.release()
+        if self._pending is not None:
+            self._pending.release()
+        self._buf = None
+        self._pending = None
+        self.disposed = True
+
+
+class CudaBackend:
+    """The device backend (one per device ordinal, like bridge.ts:8-12 for WebGPU)."""
+
+    name = "cuda"
+
+    def __init__(self, device: Device):
+        self.device = device
+        self._scopes: list[set] = []
+
+    # ---- bookkeeping -----------------------------------------------------------------------
+    def supports(self, dtype: str) -> bool:
+        return dtype in ("f32", "f16", "bf16", "i32", "bool")
+
+    def _make(self, shape, dtype, buf=None, pending=None) -> CudaTensor:
+        t = CudaTensor(self, shape, dtype, buf, pending)
+        if self._scopes:
+            self._scopes[-1].add(t)
+        return t
+
+    def _alloc(self, shape, dtype) -> CudaTensor:
+        n = 1
+        for s in shape:
+            n *= int(s)
+        return self._make(shape, dtype, self.device.alloc(n * F.DTYPE_BYTES[F.DTYPE_CODES[dtype]]))
+
+    @staticmethod
+    def _check_live(*ts):
+        for t in ts:
+            if t is not None and t.disposed:
+                raise RuntimeError("tensor-cuda: tensor used after dispose")
+
+    # ---- transfers / lifetime ----------------------------------------------------------------
+    async def fromHost(self, h: HostTensor) -> CudaTensor:
+        return self.from_host_sync(h)
+
+    def from_host_sync(self, h: HostTensor) -> CudaTensor:
+        if not self.supports(h.dtype):
+            raise TypeError(f"tensor-cuda: fromHost: unsupported dtype {h.dtype}")
+        n = 1
+        for s in h.shape:
+            n *= int(s)
+        data = np.ascontiguousarray(h.data).reshape(-1)
+        if data.size != n:
+            raise ValueError(f"tensor-cuda: fromHost {data.size} values for shape [{','.join(map(str, h.shape))}]")
+        if h.dtype == "bool":
+            data = (data != 0).astype(np.uint8)
+        else:
+            data = data.astype(STORAGE[h.dtype], copy=False)
+        t = self._alloc(h.shape, h.dtype)
+        if n:
+            self.device.copy_h2d(t._buf.ptr, data)
+            self.device.stream_sync()  # the host buffer may change after the call returns
+        return t
+
+    async def read(self, t: CudaTensor) -> HostTensor:
+        return self.read_sync(t)
+
+    def read_sync(self, t: CudaTensor) -> HostTensor:
+        self._check_live(t)
+        ptr = t.ptr
+        out = np.empty(t.size, dtype=STORAGE[t.dtype])
+        if t.size:
+            self.device.copy_d2h_into(out, ptr)
+            self.device.stream_sync()
+        return HostTensor(t.dtype, t.shape, out)
+
+    def dispose(self, t: CudaTensor) -> None:
+        t._release()
+
+    def scope(self, fn):
+        created: set = set()
+        self._scopes.append(created)
+        try:
+            result = fn()
+        except BaseException:
+            self._scopes.pop()
+            for t in created:
+                t._release()
+            raise
+        self._scopes.pop()
+        keep = set()
+
+        def visit(v):
+            if isinstance(v, CudaTensor):
+                keep.add(v)
+
+        if isinstance(result, CudaTensor):
+            keep.add(result)
+        elif isinstance(result, (list, tuple)):
+            for v in result:
+                visit(v)
+        elif isinstance(result, dict):
+            for v in result.values():
+                visit(v)
+        parent = self._scopes[-1] if self._scopes else None
+        for t in created:
+            if t in keep:
+                if parent is not None:
+                    parent.add(t)
+            else:
+                t._release()
+        return result
+
+    def flush(self, *ts) -> None:
+        for t in ts:
+            _ = t.ptr
+        self.device.stream_sync()
+
+    def destroy(self) -> None:
+        for s in self._scopes:
+            for t in s:
+                t._release()
+        self._scopes.clear()
+
+    # ---- shape / dtype -----------------------------------------------------------------------
+    def reshape(self, x: CudaTensor, shape) -> CudaTensor:
+        self._check_live(x)
+        shape = list(shape)
+        if shape.count(-1) > 1:
+            raise ValueError("tensor-cuda: reshape allows one -1")
+        if -1 in shape:
+            known = 1
+            for s in shape:
+                if s != -1:
+                    known *= s
+            if known == 0 or x.size % known:
+                raise ValueError(f"tensor-cuda: reshape [{','.join(map(str, x.shape))}] to {shape}")
+            shape[shape.index(-1)] = x.size // known
+        n = 1
+        for s in shape:
+            n *= s
+        if n != x.size:
+            raise ValueError(f"tensor-cuda: reshape [{','.join(map(str, x.shape))}] to {shape}")
+        _ = x.ptr
+        return self._make(shape, x.dtype, x._buf.retain())  # a view sharing the buffer
+
+    def cast(self, x: CudaTensor, dtype: str) -> CudaTensor:
+        self._check_live(x)
+        if dtype == x.dtype:
+            return self.reshape(x, x.shape)
+        if x.dtype not in FLOAT or dtype not in FLOAT:
+            raise NotImplementedError(f"tensor-cuda: cast {x.dtype} -> {dtype} (float <-> float only)")
+        out = self._alloc(x.shape, dtype)
+        F.call("mpc_cast", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(out._buf.ptr),
+               F.DTYPE_CODES[dtype], x.size, None)
+        return out
+
+    # ---- element-wise ------------------------------------------------------------------------
+    def add(self, x: CudaTensor, y: CudaTensor) -> CudaTensor:
+        self._check_live(x, y)
+        if x.dtype != y.dtype:
+            raise TypeError(f"tensor-cuda: add: dtype mismatch {x.dtype} vs {y.dtype} (no implicit promotion)")
+        if x.dtype not in FLOAT:
+            raise NotImplementedError("tensor-cuda: add: float dtypes only")
+        if x.size < y.size:  # add is commutative: keep the larger operand first
+            x, y = y, x
+        pg = x._pending
+        bias_like = pg is not None and not (pg.epilogue & (F.EPI_BIAS | F.EPI_GELU)) and y.size == pg.n and \
+            all(s == 1 for s in y.shape[:-1]) and y.shape[-1] == pg.n and len(y.shape) <= len(x.shape)
+        if bias_like:  # fold the bias row into the pending GEMM's epilogue
+            _ = y.ptr
+            folded = replace(pg, bias=y._buf, bias_dtype=y.dtype, epilogue=pg.epilogue | F.EPI_BIAS).retain()
+            return self._make(x.shape, x.dtype, pending=folded)
+        n_x, n_y = P.add_plan(x.shape, y.shape)
+        out = self._alloc(x.shape, x.dtype)
+        F.call("mpc_add", self.device.handle, C.c_void_p(x.ptr), C.c_void_p(y.ptr), C.c_void_p(out._buf.ptr),
+               F.DTYPE_CODES[x.dtype], n_x, n_y, None)
+        return out
+
+    def gelu(self, x: CudaTensor) -> CudaTensor:
+        self._check_live(x)
+        if x.dtype not in FLOAT:
+            raise TypeError(f"tensor-cuda: gelu: float dtypes only, got {x.dtype}")
+        pg = x._pending
+        if pg is not None and not (pg.epilogue & F.EPI_GELU):  # fold into the pending GEMM
+            return self._make(x.shape, x.dtype, pending=replace(pg, epilogue=pg.epilogue | F.EPI_GELU).retain())
+        out = self._alloc(x.shape, x.dtype)
+        F.call("mpc_gelu", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(out._buf.ptr),
+               F.DTYPE_CODES[x.dtype], x.size, None)
+        return out
+
+    def softmax(self, x: CudaTensor, axis: int = -1) -> CudaTensor:
+        """Stable softmax along ``axis`` (softmaxAxis, kernels.ts:219-247); f32 result for f32 input,
+        the input's dtype otherwise."""
+        self._check_live(x)
+        if x.dtype not in FLOAT:
+            raise TypeError(f"tensor-cuda: softmax: float dtypes only, got {x.dtype}")
+        nd = len(x.shape)
+        if not -nd <= axis < nd:
+            raise ValueError(f"tensor-cuda: softmax: axis {axis} out of range")
+        ax = axis % nd
+        outer = int(np.prod(x.shape[:ax])) if ax else 1
+        inner = int(np.prod(x.shape[ax + 1:])) if ax + 1 < nd else 1
+        out = self._alloc(x.shape, "f32")
+        F.call("mpc_softmax", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(out._buf.ptr),
+               outer, x.shape[ax], inner, None)
+        if x.dtype != "f32":
+            res = self.cast(out, x.dtype)
+            out._release()
+            return res
+        return out
+
+    # ---- contractions --------------------------------------------------------------------------
+    def matmul(self, a: CudaTensor, b: CudaTensor, out_dtype: str | None = None) -> CudaTensor:
+        """[..., m, k] @ [..., k, n] with broadcast batch axes (Tensor.matmul); the result keeps the
+        operands' dtype unless ``out_dtype`` asks otherwise (f32 accumulation either way)."""
+        self._check_live(a, b)
+        if a.dtype != b.dtype:
+            raise TypeError(f"tensor-cuda: matmul: dtype mismatch {a.dtype} vs {b.dtype} (no implicit promotion; cast() first)")
+        if a.dtype not in FLOAT:
+            raise NotImplementedError("tensor-cuda: matmul: float dtypes only")
+        pl = P.matmul_plan(a.shape, b.shape)
+        _, _ = a.ptr, b.ptr
+        pg = _PendingGemm(a._buf, b._buf, a.dtype, F.B_KN, pl.m, pl.n, pl.k, pl.batch_shape, pl.a_batch_strides,
+                          pl.b_batch_strides).retain()
+        return self._make(pl.out_shape, out_dtype or a.dtype, pending=pg)
+
+    def linear(self, x: CudaTensor, w: CudaTensor, bias: CudaTensor | None = None, activation: str | None = None,
+               out_dtype: str | None = None) -> CudaTensor:
+        """x · wᵀ (+ bias) with w [out, in] (linearNT); ``activation="gelu"`` fuses the exact GELU."""
+        self._check_live(x, w, bias)
+        rows, n_in, n_out, out_shape = P.linear_plan(x.shape, w.shape, bias.shape if bias is not None else None)
+        if x.dtype != w.dtype:
+            raise TypeError(f"tensor-cuda: linear: dtype mismatch {x.dtype} vs {w.dtype}")
+        epi = F.EPI_BIAS if bias is not None else 0
+        if activation == "gelu":
+            epi |= F.EPI_GELU
+        elif activation is not None:
+            raise ValueError(f"tensor-cuda: linear: unknown activation {activation}")
+        _, _ = x.ptr, w.ptr
+        if bias is not None:
+            _ = bias.ptr
+        pg = _PendingGemm(x._buf, w._buf, x.dtype, F.B_NK, rows, n_out, n_in, (), (), (),
+                          bias._buf if bias is not None else None, bias.dtype if bias is not None else "f32",
+                          epi).retain()
+        return self._make(out_shape, out_dtype or x.dtype, pending=pg)
+
+    def _run_gemm(self, t: CudaTensor) -> None:
+        pg = t._pending
+        bias_ptr = None
+        tmp = None
+        if pg.bias is not None:
+            bias_ptr = pg.bias.ptr
+            if pg.bias_dtype != "f32":  # the epilogue reads an f32 bias row
+                tmp = self.device.alloc(pg.n * 4)
+                F.call("mpc_cast", self.device.handle, C.c_void_p(bias_ptr), F.DTYPE_CODES[pg.bias_dtype],
+                       C.c_void_p(tmp.ptr), F.F32, pg.n, None)
+                bias_ptr = tmp.ptr
+        out = self.device.alloc(t.nbytes)
+        desc = gemm_desc(pg.m, pg.n, pg.k, F.DTYPE_CODES[pg.dtype_in], F.DTYPE_CODES[t.dtype], pg.b_layout,
+                         pg.epilogue, 1.0, pg.batch_shape, pg.a_strides, pg.b_strides)
+        self.device.gemm(desc, pg.a.ptr, pg.b.ptr, out.ptr, bias_ptr)
+        if tmp is not None:
+            tmp.release()
+        pg.release()
+        t._buf = out
+        t._pending = None
+
+    def sdpa(self, q: CudaTensor, k: CudaTensor, v: CudaTensor, mask: CudaTensor | None, scale: float,
+             causal: bool = False, lse: bool = False):
+        """softmax(scale·QKᵀ + mask)·V (attention, nn-kernels.ts:179-239). ``causal=True`` is the
+        lower-triangular bool mask without materialising it; ``lse=True`` also returns the f32
+        log-sum-exp per row."""
+        self._check_live(q, k, v, mask)
+        if not (q.dtype == k.dtype == v.dtype) or q.dtype not in FLOAT:
+            raise TypeError("tensor-cuda: sdpa: q, k, v must share a float dtype")
+        pl = P.sdpa_plan(q.shape, k.shape, v.shape, mask.shape if mask is not None else None)
+        kind = F.MASK_NONE
+        if mask is not None:
+            kind = F.MASK_BOOL if mask.dtype == "bool" else F.MASK_ADD
+            if kind == F.MASK_ADD and mask.dtype != "f32":
+                raise TypeError("tensor-cuda: sdpa: additive masks are f32")
+        out = self._alloc((pl.b, pl.h, pl.lq, pl.dv), q.dtype)
+        lse_t = self._alloc((pl.b, pl.h, pl.lq), "f32") if lse else None
+        desc = sdpa_desc(pl.b, pl.h, pl.hk, pl.lq, pl.lk, pl.d, pl.dv, F.DTYPE_CODES[q.dtype], causal, scale, kind,
+                         pl.mask_strides)
+        self.device.sdpa(desc, q.ptr, k.ptr, v.ptr, mask.ptr if mask is not None else None, out._buf.ptr,
+                         lse_t._buf.ptr if lse_t is not None else None)
+        return (out, lse_t) if lse else out
+
+    def layerNorm(self, x: CudaTensor, weight: CudaTensor | None, bias: CudaTensor | None, eps: float = 1e-5):
+        self._check_live(x, weight, bias)
+        d = x.shape[-1]
+        ws = []
+        for t in (weight, bias):
+            if t is not None and t.dtype != "f32":
+                t = self.cast(t, "f32")
+            ws.append(t)
+        out = self._alloc(x.shape, x.dtype)
+        F.call("mpc_layer_norm", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype],
+               C.c_void_p(ws[0].ptr if ws[0] is not None else None), C.c_void_p(ws[1].ptr if ws[1] is not None else None),
+               C.c_float(eps), C.c_void_p(out._buf.ptr), F.DTYPE_CODES[x.dtype], x.size // d if d else 0, d, None)
+        return out
+
+    def embedding(self, table: CudaTensor, ids: CudaTensor) -> CudaTensor:
+        self._check_live(table, ids)
+        if len(table.shape) != 2:
+            raise ValueError("tensor-cuda: embedding table must be [V, D]")
+        if ids.dtype != "i32":
+            raise TypeError("tensor-cuda: embedding ids are i32")
+        V, D = table.shape
+        out = self._alloc(ids.shape + (D,), table.dtype)
+        bad = C.c_int64(-1)
+        rc = F.load().mpc_embedding(self.device.handle, C.c_void_p(table.ptr), F.DTYPE_CODES[table.dtype],
+                                    C.c_void_p(ids.ptr), C.c_void_p(out._buf.ptr), ids.size, V, D, C.byref(bad), None)
+        if rc == F.ERR_INVALID and bad.value >= 0:
+            raise IndexError(f"tensor-cuda: embedding: id at position {bad.value} out of range [0, {V})")
+        F.check(rc, "mpc_embedding")
+        return out

@@ -14,16 +14,28 @@ from . import _ffi as F
 
 
 class DeviceBuffer:
-    """A block of device memory from the library's caching allocator (freed on dispose / GC)."""
+    """A block of device memory from the library's caching allocator, reference-counted: views
+    and pending work retain it; it returns to the allocator when the last holder releases it
+    (or on garbage collection)."""
 
-    __slots__ = ("device", "ptr", "nbytes", "__weakref__")
+    __slots__ = ("device", "ptr", "nbytes", "refs", "__weakref__")
 
     def __init__(self, device: "Device", nbytes: int):
         self.device = device
         self.nbytes = int(nbytes)
+        self.refs = 1
         p = C.c_void_p()
         F.call("mpc_alloc", device.handle, max(self.nbytes, 1), C.byref(p))
         self.ptr = p.value
+
+    def retain(self) -> "DeviceBuffer":
+        self.refs += 1
+        return self
+
+    def release(self) -> None:
+        self.refs -= 1
+        if self.refs <= 0:
+            self.free()
 
     def free(self) -> None:
         if self.ptr is not None and self.device.handle is not None:
