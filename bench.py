@@ -15,6 +15,11 @@ A step is one pass of the hot path over one batch of synthetic input:
                                (+ f32 log-sum-exp): Backend.sdpa (index.ts:821-840) as one kernel.
   gemm_f32_1024                one f32 1024^3 GEMM (3xTF32 on the tensor cores); L2 is flushed
                                between timed steps (the inputs are 8 MiB).
+  nsplit_gemm_bf16             C[16384,65536] = A[16384,8192] @ B[8192,65536] bf16 -> bf16 with B's
+                               columns split over the N ranks (strong scaling: the total work is
+                               fixed); each rank's GEMM epilogue stores its blocks into every rank's
+                               copy of C over NVLink (the all-gather fused into the GEMM). The line
+                               also carries the GEMM-only and GEMM + NCCL all-gather + permute times.
 
 ``value`` is device-timed throughput with inputs resident in HBM (CUDA events on the launching
 stream, barrier + synchronize around the timed region, max over ranks). ``e2e`` runs the same
@@ -46,6 +51,10 @@ WORKLOADS = {
                               desc="batched GEMM bf16 in / f32 accumulate+out, 64x2048^3, +bias[2048], exact GELU"),
     "gemm_f32_1024": dict(kind="gemm", batch=1, m=1024, n=1024, k=1024, dtype="f32", out="f32", epilogue="none",
                           metric="GEMM TFLOP/s (f32, 3xTF32)", desc="single f32 GEMM 1024^3 (3xTF32 on tcgen05)"),
+    "nsplit_gemm_bf16": dict(kind="nsplit", batch=1, m=16384, n=65536, k=8192, dtype="bf16", out="bf16",
+                             epilogue="none", metric="GEMM TFLOP/s (column-split bf16 GEMM + all-gather)",
+                             desc="C[16384,65536] = A[16384,8192] @ B[8192,65536] bf16, B's columns split over "
+                                  "the ranks, every rank ends with the whole C (GEMM fused with its all-gather)"),
     "causal_attention_f16": dict(kind="attention", batch=16, heads=32, seq=2048, head_dim=128, dtype="f16",
                                  causal=True, metric="fused attention TFLOP/s (causal f16)",
                                  desc="causal sdpa f16 [16,32,2048,128], scale 1/sqrt(128), f16 out + f32 LSE"),
@@ -154,7 +163,7 @@ def dist_env():
 
 
 def flop_per_step(w):
-    if w["kind"] == "gemm":
+    if w["kind"] in ("gemm", "nsplit"):
         return 2.0 * w["batch"] * w["m"] * w["n"] * w["k"]
     f = 4.0 * w["batch"] * w["heads"] * w["seq"] * w["seq"] * w["head_dim"]
     return f / 2 if w["causal"] else f
@@ -190,7 +199,8 @@ def cpu_sample_rate(w: dict, target_s: float, threads: int):
         # applied element-wise); the rate is reported against the same causal FLOP count as the GPU
         flop = flop_per_step(w) / heads_total * nh
         return flop / dt, f"{nh} of the {heads_total} (b,h) heads [{L}x{D}], f64 accumulate", dt
-    m, n, k = w["m"], w["n"], w["k"]
+    m, n_all, k = w["m"], w["n"], w["k"]
+    n = min(n_all, 4096)  # a column block of a very wide B has the same per-FLOP cost
     b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
     bias = (rng.standard_normal(n) * 0.02).astype(np.float32)
 
@@ -212,10 +222,11 @@ def cpu_sample_rate(w: dict, target_s: float, threads: int):
     reps = max(1, min(w["batch"], want_rows // m)) if want_rows > m else 1
     t = sum(run(rows) for _ in range(reps))
     flop = 2.0 * reps * rows * n * k
-    what = (f"{reps} of the {w['batch']} products ({m}x{k} @ {k}x{n}" if rows == m else
-            f"{rows} of the {m} rows of one {m}x{k} @ {k}x{n} product (")
-    return flop / t, what + ("+bias, GELU), f64 accumulate" if w["epilogue"] == "bias+gelu"
-                             else "), f64 accumulate"), t
+    cols = f"{k}x{n}" if n == n_all else f"{k}x{n} column block of the {k}x{n_all}"
+    what = (f"{reps} of the {w['batch']} products {m}x{k} @ {cols}" if rows == m else
+            f"{rows} of the {m} rows of one {m}x{k} @ {cols} product")
+    return flop / t, what + (" (+bias, GELU), f64 accumulate" if w["epilogue"] == "bias+gelu"
+                             else ", f64 accumulate"), t
 
 
 def run_reference(args, w):
@@ -233,7 +244,8 @@ def run_reference(args, w):
     line = {
         "impl": "reference", "metric": w["metric"], "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": flop_per_step(w) / (v * 1e12) * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 (f32 storage)",
+        "higher_is_better": True, "scaling": "strong" if w["kind"] == "nsplit" else "weak", "vs_baseline": None,
+        "dtype": "f64 (f32 storage)",
         "data": "synthetic", "config": {"workload": args.workload, "description": w["desc"]},
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": "per step: " + sample + "; the oracle's restatement of tensor-core "
@@ -288,6 +300,43 @@ def setup_attention(w, dev, torch, g, local, F):
     return [q, k, v], out, launch, f"attn_kernel<D={D}> (2 Q tiles x 128 rows per CTA, 10 warps)"
 
 
+def setup_nsplit(w, dev, torch, g, local, F, world, pg):
+    from tensor_cuda import plan as P
+    from tensor_cuda.parallel import ColumnSplitGemm, PeerGroup, unique_id
+    from tensor_cuda.runtime import gemm_desc
+    pl = P.column_split_plan(w["m"], w["n"], w["k"], world, w["out"])
+    M, n, K = w["m"], pl.n_shard, w["k"]
+    dvc = f"cuda:{local}"
+    A = (torch.randn((M, K), generator=g, device=dvc) / K ** 0.5).to(torch.bfloat16)
+    Bs = (torch.randn((K, n), generator=g, device=dvc) / K ** 0.5).to(torch.bfloat16)  # this rank's columns
+    group = PeerGroup.from_torch(dev) if world > 1 else PeerGroup(dev, 0, 1, unique_id())
+    fused = ColumnSplitGemm(group, M, n, K, "bf16", w["out"], F.B_KN, fused=True)
+
+    class Out:  # this rank's whole C, in the peer buffer
+        ptr = fused.out_ptr
+        nbytes = M * w["n"] * F.DTYPE_BYTES[F.DTYPE_CODES[w["out"]]]
+
+    def launch(ptrs, optr, stream):
+        fused(ptrs[0], ptrs[1], stream)
+
+    extras = {"group": group, "fused": fused, "pl": pl,
+              "gemm_desc": gemm_desc(M, n, K, F.BF16, F.DTYPE_CODES[w["out"]], F.B_KN)}
+    return [A, Bs], Out, launch, "gemm_kernel<kHalf, B MN-major, BN=256, 4 stages, 8 output maps>", extras
+
+
+def time_region(dev, stream, fn, steps, barrier):
+    barrier()
+    dev.stream_sync(stream)
+    e0, e1 = dev.event(), dev.event()
+    dev.record(e0, stream)
+    for _ in range(steps):
+        fn()
+    dev.record(e1, stream)
+    dev.stream_sync(stream)
+    barrier()
+    return dev.elapsed_ms(e0, e1) / steps
+
+
 def run_ours(args, w):
     import numpy as np
     import torch
@@ -313,8 +362,14 @@ def run_ours(args, w):
     stream = dev.stream
     g = torch.Generator(device=f"cuda:{local}")
     g.manual_seed(1234 + rank)
-    setup = setup_gemm if w["kind"] == "gemm" else setup_attention
-    ins, out, launch, kernel_name = setup(w, dev, torch, g, local, F)
+    extras = {}
+    if w["kind"] == "nsplit":
+        g.manual_seed(1234)  # A is the same on every rank
+        ins, out, launch, kernel_name, extras = setup_nsplit(w, dev, torch, g, local, F, world, pg)
+    else:
+        setup = setup_gemm if w["kind"] == "gemm" else setup_attention
+        ins, out, launch, kernel_name = setup(w, dev, torch, g, local, F)
+    strong = w["kind"] == "nsplit"
     torch.cuda.synchronize()
     ptrs = [t.data_ptr() for t in ins]
     flop_step = flop_per_step(w)
@@ -363,12 +418,36 @@ def run_ours(args, w):
     barrier()
     launches = dev.launch_count() - launches0
     clocks = sampler.stop()
-    if pg:
-        t = torch.tensor([ms_total], device=f"cuda:{local}", dtype=torch.float64)
+    def max_over_ranks(x):
+        if not pg:
+            return x
+        t = torch.tensor([x], device=f"cuda:{local}", dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms_total = float(t.item())
+        return float(t.item())
+
+    ms_total = max_over_ranks(ms_total)
     ms_step = ms_total / args.steps
-    value = flop_step * world / (ms_step * 1e-3) / 1e12
+    job_flop = flop_step if strong else flop_step * world
+    value = job_flop / (ms_step * 1e-3) / 1e12
+
+    breakdown = None
+    if strong:  # the same step as GEMM alone and as GEMM + NCCL all-gather + permute
+        from tensor_cuda.parallel import ColumnSplitGemm
+        local_c = dev.alloc(extras["pl"].n_shard * w["m"] * F.DTYPE_BYTES[F.DTYPE_CODES[w["out"]]])
+        gd = extras["gemm_desc"]
+        gemm_only = lambda: dev.gemm(gd, ptrs[0], ptrs[1], local_c.ptr, None, stream)
+        nccl = ColumnSplitGemm(extras["group"], w["m"], extras["pl"].n_shard, w["k"], "bf16", w["out"], F.B_KN,
+                               fused=False)
+        nccl_step = lambda: nccl(ptrs[0], ptrs[1], stream)
+        for fn in (gemm_only, nccl_step):
+            for _ in range(max(1, args.warmup)):
+                fn()
+        breakdown = {"fused_gemm_allgather": ms_step,
+                     "gemm_only": max_over_ranks(time_region(dev, stream, gemm_only, args.steps, barrier)),
+                     "gemm_then_nccl_allgather_then_permute": max_over_ranks(
+                         time_region(dev, stream, nccl_step, args.steps, barrier))}
+        nccl.destroy()
+        local_c.free()
 
     # ---- e2e: through the C ABI from pinned host buffers, copies inside the timed region ----
     e2e = None
@@ -397,12 +476,8 @@ def run_ours(args, w):
         dev.record(x1, stream)
         dev.stream_sync(stream)
         barrier()
-        ms_e2e = dev.elapsed_ms(x0, x1)
-        if pg:
-            t = torch.tensor([ms_e2e], device=f"cuda:{local}", dtype=torch.float64)
-            pg.all_reduce(t, op=pg.ReduceOp.MAX)
-            ms_e2e = float(t.item())
-        e2e = {"value": flop_step * world / (ms_e2e / args.e2e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
+        ms_e2e = max_over_ranks(dev.elapsed_ms(x0, x1))
+        e2e = {"value": job_flop / (ms_e2e / args.e2e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": int(sum(h.nbytes for h, _, _ in hins)), "d2h_bytes_per_step": int(hout.nbytes),
                "ms_per_step": ms_e2e / args.e2e_steps,
                "path": "mpc_memcpy_h2d_async per input -> one kernel -> mpc_memcpy_d2h_async, pinned host buffers"}
@@ -414,11 +489,21 @@ def run_ours(args, w):
         peaks = load_peaks()
         long_region = ms_total > 2000
         peak = peaks["bf16_tflops_sustained"] if long_region else peaks["bf16_tflops"]
-        achieved = flop_step / (ms_step * 1e-3) / 1e12  # one launch of the kernel per step
+        rank_flop = flop_step / world if strong else flop_step
+        achieved = rank_flop / (ms_step * 1e-3) / 1e12  # one launch of the kernel per step and rank
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "peak_source": f"{peaks['source']} bf16 dense ({'sustained' if long_region else 'burst'})",
-                "traffic": profiled_traffic(args.workload), "algorithmic_flop_per_launch": flop_step,
+                "traffic": profiled_traffic(args.workload), "algorithmic_flop_per_launch": rank_flop,
                 "kernel": kernel_name}
+        if strong and world > 1:
+            # fused GEMM + all-gather: the slower of the tensor-core time and the NVLink time of the
+            # bytes every GPU must receive ((p-1)/p of C), at the measured 770 GB/s per direction
+            c_bytes = out.nbytes
+            nv_bytes = c_bytes * (world - 1) / world
+            target_ms = max(rank_flop / (peak * 1e12), nv_bytes / 770e9) * 1e3
+            roof["nvlink"] = {"bytes_in_per_gpu": nv_bytes, "achieved_gbs": nv_bytes / (ms_step * 1e-3) / 1e9,
+                              "peak_gbs": 770.0, "peak_source": "measured peer copy per direction",
+                              "target_ms": target_ms, "frac_of_target": target_ms / ms_step}
         if w.get("dtype") == "f32":
             roof["note"] = "3xTF32 issues 3 tf32 MMAs per product; tf32 dense peak is half of bf16"
         if w["kind"] == "attention" and w["causal"]:
@@ -432,18 +517,26 @@ def run_ours(args, w):
                        "sample": sample + f" ({secs:.1f} s); the oracle's restatement of the reference's CPU path"}
             except Exception as ex:  # reported, never required
                 cpu = {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
-        cfg = {"workload": args.workload, "description": w["desc"], "parallelism": f"dp{world} (shards, no collective)"}
+        par = (f"column split over {world} GPUs, all-gather fused into the GEMM epilogue (peer stores)" if strong
+               else f"dp{world} (shards, no collective)")
+        cfg = {"workload": args.workload, "description": w["desc"], "parallelism": par}
+        if breakdown:
+            cfg["breakdown_ms_per_step"] = breakdown
         cfg.update({k: w[k] for k in ("batch", "m", "n", "k", "heads", "seq", "head_dim", "out") if k in w})
         cfg["l2"] = "flushed between steps (256 MiB write)" if flush is not None else "inputs larger than L2 (126 MB)"
         line = {
             "metric": w["metric"], "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "strong" if strong else "weak",
             "vs_baseline": None, "dtype": w["dtype"],
             "data": "synthetic (seeded torch RNG on device; configuration shapes and distributions)",
             "config": cfg, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    if extras:
+        extras["fused"].destroy()
+        extras["group"].destroy()
     if pg:
         pg.destroy_process_group()
 

@@ -191,6 +191,12 @@ int mpc_embedding(mpc_device *dev, const void *table, int32_t dtype, const int32
 int mpc_cast(mpc_device *dev, const void *x, int32_t dtype_in, void *out, int32_t dtype_out, int64_t n,
              mpc_stream s);
 
+/* Axis permutation of a contiguous tensor of up to 6 axes: out has shape shape[perm[k]]
+ * (Backend.transpose, packages/tensor-cpu/src/device-array.ts:459-471; also the head split /
+ * merge of attention and the reassembly of a column-split GEMM). */
+int mpc_transpose(mpc_device *dev, const void *x, void *out, int32_t elem_bytes, int32_t rank, const int64_t *shape,
+                  const int32_t *perm, mpc_stream s);
+
 /* ---- multi-GPU: NCCL over NVLink, one rank per process (no reference counterpart) ---------- */
 int mpc_comm_unique_id(void *id128);
 int mpc_comm_init(mpc_device *dev, int nranks, int rank, const void *id128, mpc_comm **comm);
@@ -198,6 +204,31 @@ int mpc_comm_destroy(mpc_comm *comm);
 int mpc_comm_abort(mpc_comm *comm);
 /* Gathers `bytes` from every rank into recv (rank r's block at offset r*bytes). */
 int mpc_allgather(mpc_comm *comm, const void *send, void *recv, size_t bytes, mpc_stream s);
+
+/* ---- peer memory and the GEMM fused with its all-gather (no reference counterpart) ----------
+ * A peer buffer is one device allocation per rank of a communicator, every rank's allocation
+ * mapped into every process (CUDA IPC over NVLink). Creating and destroying one are collective:
+ * every rank calls them, in the same order. mpc_peer_barrier queues a device-side barrier over
+ * the group on stream s; a rank that does not arrive within the device's wait timeout makes the
+ * next synchronisation return MPC_ERR_TIMEOUT. */
+typedef struct mpc_peer_buffer mpc_peer_buffer;
+int mpc_peer_buffer_create(mpc_comm *comm, size_t bytes, mpc_peer_buffer **buf);
+int mpc_peer_buffer_ptr(mpc_peer_buffer *buf, int rank, void **ptr);
+int mpc_peer_barrier(mpc_peer_buffer *buf, mpc_stream s);
+int mpc_peer_buffer_destroy(mpc_peer_buffer *buf);
+/* The product of desc (f16 / bf16 operands) stored into ndst (1..8) row-major matrices with row
+ * pitch ldc elements, at columns col_offset .. col_offset + n - 1 of each. ldc and col_offset in
+ * bytes and every destination address must be multiples of 16. */
+int mpc_gemm_multi_store(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B,
+                         const float *bias, void *const *dsts, int32_t ndst, int64_t ldc, int64_t col_offset,
+                         mpc_stream s);
+/* Column-split GEMM with its all-gather in one kernel: rank r of p computes A [m, k] times its
+ * column block B_r (desc->n = n columns) and the epilogue writes each output block into every
+ * rank's C buffer, so that on return (in stream order) every rank's buffer holds the whole
+ * row-major C [m, p*n], rank r's block at columns r*n .. r*n + n - 1. A peer barrier precedes
+ * the GEMM (no rank still reads the previous C) and follows it (all blocks have landed). */
+int mpc_gemm_allgather(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B,
+                       const float *bias, mpc_peer_buffer *C, mpc_stream s);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

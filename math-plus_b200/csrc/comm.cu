@@ -58,12 +58,6 @@ int nccl_fail(ncclResult_t r, const char *what) {
 }  // namespace
 }  // namespace mpc
 
-struct mpc_comm {
-  mpc_device *dev;
-  mpc::ncclComm_t comm;
-  int nranks, rank;
-};
-
 using namespace mpc;
 
 extern "C" {

@@ -50,11 +50,16 @@ struct Params {
   uint32_t idesc;  // tcgen05 instruction descriptor (operand format, B major, M, N)
   int *err;
   unsigned long long timeout_ns;
+  int ndst;  // output maps in use (1 unless the product is stored to several matrices)
 };
 
-struct Maps {
-  CUtensorMap a, b, a_lo, b_lo, c;
+// The operand maps and NDST output maps; each 32 x 32 output block is stored through c[0..ndst).
+template <int NDST>
+struct MapsT {
+  CUtensorMap a, b, a_lo, b_lo, c[NDST];
 };
+using Maps = MapsT<1>;
+constexpr int kMaxDst = 8;
 
 template <int KIND, bool B_MN, int BN, int STAGES>
 struct Cfg {
@@ -160,8 +165,8 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], in
   }
 }
 
-template <int KIND, bool B_MN, int BN, int STAGES>
-__global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Maps maps, const Params p) {
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST>
+__global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ MapsT<NDST> maps, const Params p) {
   using C = Cfg<KIND, B_MN, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&maps.a);
     tma_prefetch_desc(&maps.b);
-    tma_prefetch_desc(&maps.c);
+    tma_prefetch_desc(&maps.c[0]);
     if constexpr (KIND == kTF32x3) {
       tma_prefetch_desc(&maps.a_lo);
       tma_prefetch_desc(&maps.b_lo);
@@ -359,12 +364,22 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if (row0 < p.M && col0 < p.N) tma_store_3d(&maps.c, buf, col0, row0, b);
+          if (row0 < p.M && col0 < p.N) {
+#pragma unroll
+            for (int d = 0; d < NDST; ++d)
+              if (d < p.ndst) tma_store_3d(&maps.c[d], buf, col0, row0, b);
+          }
           tma_store_commit();
         }
       }
     }
-    if (lane == 0) tma_store_wait_all<0>();
+    if (lane == 0) {
+      tma_store_wait_all<0>();
+      if constexpr (NDST > 1) {  // blocks stored to other GPUs are visible system-wide at kernel end
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence_system();
+      }
+    }
     __syncwarp();
   }
 
@@ -437,10 +452,10 @@ __global__ void fill_epilogue_kernel(void *C, int out_dtype, int64_t rows, int64
   }
 }
 
-template <int KIND, bool B_MN, int BN, int STAGES>
-int launch(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1>
+int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream_t st) {
   using C = Cfg<KIND, B_MN, BN, STAGES>;
-  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES>;
+  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST>;
   static bool configured[64] = {};
   const int ord = dev->ordinal & 63;
   if (!configured[ord]) {
@@ -469,40 +484,155 @@ static CUtensorMapDataType tmap_dtype(int dt) {
 
 static inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
+namespace gemm {
+
+// What the descriptor implies once validated: the batch extent, the number of distinct A / B
+// matrices the batch strides reach, and the kernel configuration.
+struct Prep {
+  int64_t batch = 1, nA = 1, nB = 1;
+  bool tf32 = false, b_mn = false;
+  int BN = 256;
+};
+
+// Validates `d` and fills every kernel parameter that does not depend on the output.
+// Returns MPC_OK with prep.batch == 0 (or M / N == 0) when there is nothing to compute.
+static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, const char *who, Params &p, Prep &pr) {
+  const int64_t M = d->m, N = d->n, K = d->k;
+  if (M < 0 || N < 0 || K < 0)
+    return fail(MPC_ERR_INVALID, "%s: negative dimension m=%lld n=%lld k=%lld", who, (long long)M, (long long)N,
+                (long long)K);
+  if (d->dtype_in != MPC_F32 && d->dtype_in != MPC_F16 && d->dtype_in != MPC_BF16)
+    return fail(MPC_ERR_INVALID, "%s: dtype_in %d is not f32/f16/bf16", who, d->dtype_in);
+  if (d->dtype_out != MPC_F32 && d->dtype_out != MPC_F16 && d->dtype_out != MPC_BF16)
+    return fail(MPC_ERR_INVALID, "%s: dtype_out %d is not f32/f16/bf16", who, d->dtype_out);
+  if (d->b_layout != MPC_B_KN && d->b_layout != MPC_B_NK) return fail(MPC_ERR_INVALID, "%s: b_layout %d", who, d->b_layout);
+  if (d->batch_rank < 0 || d->batch_rank > 4) return fail(MPC_ERR_INVALID, "%s: batch_rank %d", who, d->batch_rank);
+  if ((d->epilogue & MPC_EPI_BIAS) && !bias) return fail(MPC_ERR_INVALID, "%s: BIAS epilogue without bias", who);
+  if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return fail(MPC_ERR_UNSUPPORTED, "%s: dimension above 2^30", who);
+  p = Params{};
+  pr = Prep{};
+  p.brank = d->batch_rank;
+  for (int i = 0; i < d->batch_rank; ++i) {
+    const int64_t sz = d->batch_shape[i];
+    if (sz < 0) return fail(MPC_ERR_INVALID, "%s: batch_shape[%d] = %lld", who, i, (long long)sz);
+    pr.batch *= sz;
+    const int64_t sa = d->a_batch_stride[i], sb = d->b_batch_stride[i];
+    if (sa < 0 || sb < 0 || (M * K && sa % (M * K)) || (K * N && sb % (K * N)))
+      return fail(MPC_ERR_INVALID, "%s: batch strides must be whole matrices (axis %d: %lld, %lld)", who, i,
+                  (long long)sa, (long long)sb);
+    p.bshape[i] = (int)sz;
+    p.a_bstride[i] = M * K ? (int)(sa / (M * K)) : 0;
+    p.b_bstride[i] = K * N ? (int)(sb / (K * N)) : 0;
+    if (sz > 0) {
+      pr.nA += (sz - 1) * p.a_bstride[i];
+      pr.nB += (sz - 1) * p.b_bstride[i];
+    }
+  }
+  pr.tf32 = d->dtype_in == MPC_F32;
+  pr.b_mn = !pr.tf32 && d->b_layout == MPC_B_KN;
+  pr.BN = pr.tf32 ? 128 : 256;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.tiles_m = (int)((M + 127) / 128);
+  p.tiles_n = (int)((N + pr.BN - 1) / pr.BN);
+  const int64_t tiles = pr.batch * p.tiles_m * p.tiles_n;
+  if (tiles > INT32_MAX) return fail(MPC_ERR_UNSUPPORTED, "%s: %lld tiles", who, (long long)tiles);
+  p.tiles_total = (int)tiles;
+  p.k_blocks = (int)((K + (pr.tf32 ? 31 : 63)) / (pr.tf32 ? 32 : 64));
+  p.group_m = 16;
+  p.alpha = d->alpha;
+  p.bias = bias;
+  p.epilogue = d->epilogue & (MPC_EPI_BIAS | MPC_EPI_GELU);
+  p.idesc = make_idesc(pr.tf32 ? kFmtTF32 : (d->dtype_in == MPC_BF16 ? kFmtBF16 : kFmtF16), pr.b_mn, 128, pr.BN);
+  p.out_dtype = d->dtype_out;
+  p.err = dev->d_err;
+  p.timeout_ns = dev->timeout_ns;
+  p.ndst = 1;
+  return MPC_OK;
+}
+
+// Operand scratch: tf32 hi / lo planes, or pitch-padded copies of misaligned half operands.
+struct OperandScratch {
+  Scratch a, b, a2, b2;
+};
+
+// Builds the A / B maps (and runs the tf32 split prologue or the padding copies they need).
+template <int NDST>
+static int operand_maps(mpc_device *dev, const mpc_gemm_desc *d, const Prep &pr, const void *A, const void *B,
+                        MapsT<NDST> &maps, OperandScratch &s, cudaStream_t st) {
+  const int64_t M = d->m, N = d->n, K = d->k, nA = pr.nA, nB = pr.nB;
+  const CUtensorMapSwizzle SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  int rc;
+  if (pr.tf32) {
+    const int64_t ldk = round_up(K, 4);
+    if ((rc = s.a.get(dev, st, (size_t)(nA * M * ldk) * 4)) || (rc = s.a2.get(dev, st, (size_t)(nA * M * ldk) * 4)) ||
+        (rc = s.b.get(dev, st, (size_t)(nB * N * ldk) * 4)) || (rc = s.b2.get(dev, st, (size_t)(nB * N * ldk) * 4)))
+      return rc;
+    split_rows_kernel<<<1184, 256, 0, st>>>(static_cast<const float *>(A), (float *)s.a.ptr, (float *)s.a2.ptr,
+                                            nA * M, K, ldk);
+    dev->launches++;
+    if (d->b_layout == MPC_B_NK) {
+      split_rows_kernel<<<1184, 256, 0, st>>>(static_cast<const float *>(B), (float *)s.b.ptr, (float *)s.b2.ptr,
+                                              nB * N, K, ldk);
+    } else {
+      dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)nB);
+      split_transpose_kernel<<<g, dim3(32, 8), 0, st>>>(static_cast<const float *>(B), (float *)s.b.ptr,
+                                                         (float *)s.b2.ptr, (int)K, (int)N, (int)ldk);
+    }
+    dev->launches++;
+    if ((rc = check_launch(dev, "split_tf32"))) return rc;
+    const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    if ((rc = make_map_3d(&maps.a, f32, s.a.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
+        (rc = make_map_3d(&maps.a_lo, f32, s.a2.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
+        (rc = make_map_3d(&maps.b, f32, s.b.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)) ||
+        (rc = make_map_3d(&maps.b_lo, f32, s.b2.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)))
+      return rc;
+    return MPC_OK;
+  }
+  const size_t es = 2;
+  const CUtensorMapDataType dt = tmap_dtype(d->dtype_in);
+  // A: [nA][M][K]; a padded copy when K*2 bytes is not a multiple of 16 or A is misaligned.
+  const void *ap = A;
+  int64_t lda = K;
+  if (((uintptr_t)A & 15) || (K * es) % 16) {
+    lda = round_up(K, 8);
+    if ((rc = s.a.get(dev, st, (size_t)(nA * M * lda) * es))) return rc;
+    MPC_CUDA(dev, cudaMemcpy2DAsync(s.a.ptr, lda * es, A, K * es, K * es, nA * M, cudaMemcpyDeviceToDevice, st));
+    ap = s.a.ptr;
+  }
+  if ((rc = make_map_3d(&maps.a, dt, ap, K, M, nA, lda * es, M * lda * es, 64, 128, SW))) return rc;
+  const void *bp = B;
+  if (pr.b_mn) {  // B [nB][K][N]
+    int64_t ldb = N;
+    if (((uintptr_t)B & 15) || (N * es) % 16) {
+      ldb = round_up(N, 8);
+      if ((rc = s.b.get(dev, st, (size_t)(nB * K * ldb) * es))) return rc;
+      MPC_CUDA(dev, cudaMemcpy2DAsync(s.b.ptr, ldb * es, B, N * es, N * es, nB * K, cudaMemcpyDeviceToDevice, st));
+      bp = s.b.ptr;
+    }
+    return make_map_3d(&maps.b, dt, bp, N, K, nB, ldb * es, K * ldb * es, 64, 64, SW);
+  }
+  int64_t ldb = K;  // B [nB][N][K]
+  if (((uintptr_t)B & 15) || (K * es) % 16) {
+    ldb = round_up(K, 8);
+    if ((rc = s.b.get(dev, st, (size_t)(nB * N * ldb) * es))) return rc;
+    MPC_CUDA(dev, cudaMemcpy2DAsync(s.b.ptr, ldb * es, B, K * es, K * es, nB * N, cudaMemcpyDeviceToDevice, st));
+    bp = s.b.ptr;
+  }
+  return make_map_3d(&maps.b, dt, bp, K, N, nB, ldb * es, N * ldb * es, 64, 256, SW);
+}
+
+}  // namespace gemm
+
 int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, void *Cout, const float *bias,
              cudaStream_t st) {
   using namespace gemm;
-  const int64_t M = d->m, N = d->n, K = d->k;
-  if (M < 0 || N < 0 || K < 0) return fail(MPC_ERR_INVALID, "mpc_gemm: negative dimension m=%lld n=%lld k=%lld",
-                                           (long long)M, (long long)N, (long long)K);
-  if (d->dtype_in != MPC_F32 && d->dtype_in != MPC_F16 && d->dtype_in != MPC_BF16)
-    return fail(MPC_ERR_INVALID, "mpc_gemm: dtype_in %d is not f32/f16/bf16", d->dtype_in);
-  if (d->dtype_out != MPC_F32 && d->dtype_out != MPC_F16 && d->dtype_out != MPC_BF16)
-    return fail(MPC_ERR_INVALID, "mpc_gemm: dtype_out %d is not f32/f16/bf16", d->dtype_out);
-  if (d->b_layout != MPC_B_KN && d->b_layout != MPC_B_NK)
-    return fail(MPC_ERR_INVALID, "mpc_gemm: b_layout %d", d->b_layout);
-  if (d->batch_rank < 0 || d->batch_rank > 4) return fail(MPC_ERR_INVALID, "mpc_gemm: batch_rank %d", d->batch_rank);
-  if ((d->epilogue & MPC_EPI_BIAS) && !bias) return fail(MPC_ERR_INVALID, "mpc_gemm: BIAS epilogue without bias");
-  if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return fail(MPC_ERR_UNSUPPORTED, "mpc_gemm: dimension above 2^30");
-  int64_t batch = 1, nA = 1, nB = 1;
-  Params p{};
-  p.brank = d->batch_rank;
-  for (int i = 0; i < d->batch_rank; ++i) {
-    const int64_t s = d->batch_shape[i];
-    if (s < 0) return fail(MPC_ERR_INVALID, "mpc_gemm: batch_shape[%d] = %lld", i, (long long)s);
-    batch *= s;
-    const int64_t sa = d->a_batch_stride[i], sb = d->b_batch_stride[i];
-    if (sa < 0 || sb < 0 || (M * K && sa % (M * K)) || (K * N && sb % (K * N)))
-      return fail(MPC_ERR_INVALID, "mpc_gemm: batch strides must be whole matrices (axis %d: %lld, %lld)", i,
-                  (long long)sa, (long long)sb);
-    p.bshape[i] = (int)s;
-    p.a_bstride[i] = M * K ? (int)(sa / (M * K)) : 0;
-    p.b_bstride[i] = K * N ? (int)(sb / (K * N)) : 0;
-    if (s > 0) {
-      nA += (s - 1) * p.a_bstride[i];
-      nB += (s - 1) * p.b_bstride[i];
-    }
-  }
+  Params p;
+  Prep pr;
+  int rc = prepare(dev, d, bias, "mpc_gemm", p, pr);
+  if (rc) return rc;
+  const int64_t M = d->m, N = d->n, K = d->k, batch = pr.batch;
   if (batch == 0 || M == 0 || N == 0) return MPC_OK;
   if (!A || !B || !Cout) return fail(MPC_ERR_INVALID, "mpc_gemm: null operand pointer");
   const size_t eo = dtype_size(d->dtype_out);
@@ -511,34 +641,10 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
     dev->launches++;
     return check_launch(dev, "fill_epilogue_kernel");
   }
-
-  const bool tf32 = d->dtype_in == MPC_F32;
-  const bool b_mn = !tf32 && d->b_layout == MPC_B_KN;
-  const int BN = tf32 ? 128 : 256;
-  p.M = (int)M;
-  p.N = (int)N;
-  p.K = (int)K;
-  p.tiles_m = (int)((M + 127) / 128);
-  p.tiles_n = (int)((N + BN - 1) / BN);
-  const int64_t tiles = batch * p.tiles_m * p.tiles_n;
-  if (tiles > INT32_MAX) return fail(MPC_ERR_UNSUPPORTED, "mpc_gemm: %lld tiles", (long long)tiles);
-  p.tiles_total = (int)tiles;
-  p.k_blocks = (int)((K + (tf32 ? 31 : 63)) / (tf32 ? 32 : 64));
-  p.group_m = 16;
-  p.alpha = d->alpha;
-  p.bias = bias;
-  p.epilogue = d->epilogue & (MPC_EPI_BIAS | MPC_EPI_GELU);
-  p.idesc = make_idesc(tf32 ? kFmtTF32 : (d->dtype_in == MPC_BF16 ? kFmtBF16 : kFmtF16), b_mn, 128, BN);
-  p.out_dtype = d->dtype_out;
-  p.err = dev->d_err;
-  p.timeout_ns = dev->timeout_ns;
-
   Maps maps;
   memset(&maps, 0, sizeof(maps));
-  Scratch sa, sb, sa2, sb2, sc;
-  const CUtensorMapSwizzle SW = CU_TENSOR_MAP_SWIZZLE_128B;
-  int rc;
-
+  OperandScratch s;
+  Scratch sc;
   // Output: a padded staging matrix when the row pitch or base is not 16-byte aligned.
   void *cdst = Cout;
   int64_t ldc = N;
@@ -547,75 +653,62 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
     if ((rc = sc.get(dev, st, (size_t)(batch * M * ldc) * eo))) return rc;
     cdst = sc.ptr;
   }
-  if ((rc = make_map_3d(&maps.c, tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo, 32, 32,
+  if ((rc = make_map_3d(&maps.c[0], tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo, 32, 32,
                         eo == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
     return rc;
-
-  if (tf32) {
-    const int64_t ldk = round_up(K, 4);
-    if ((rc = sa.get(dev, st, (size_t)(nA * M * ldk) * 4)) || (rc = sa2.get(dev, st, (size_t)(nA * M * ldk) * 4)) ||
-        (rc = sb.get(dev, st, (size_t)(nB * N * ldk) * 4)) || (rc = sb2.get(dev, st, (size_t)(nB * N * ldk) * 4)))
-      return rc;
-    split_rows_kernel<<<1184, 256, 0, st>>>(static_cast<const float *>(A), (float *)sa.ptr, (float *)sa2.ptr, nA * M,
-                                            K, ldk);
-    dev->launches++;
-    if (d->b_layout == MPC_B_NK) {
-      split_rows_kernel<<<1184, 256, 0, st>>>(static_cast<const float *>(B), (float *)sb.ptr, (float *)sb2.ptr,
-                                              nB * N, K, ldk);
-    } else {
-      dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)nB);
-      split_transpose_kernel<<<g, dim3(32, 8), 0, st>>>(static_cast<const float *>(B), (float *)sb.ptr,
-                                                         (float *)sb2.ptr, (int)K, (int)N, (int)ldk);
-    }
-    dev->launches++;
-    if ((rc = check_launch(dev, "split_tf32"))) return rc;
-    const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-    if ((rc = make_map_3d(&maps.a, f32, sa.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
-        (rc = make_map_3d(&maps.a_lo, f32, sa2.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
-        (rc = make_map_3d(&maps.b, f32, sb.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)) ||
-        (rc = make_map_3d(&maps.b_lo, f32, sb2.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)))
-      return rc;
+  if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st))) return rc;
+  if (pr.tf32)
     rc = launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
-  } else {
-    const size_t es = 2;
-    const CUtensorMapDataType dt = tmap_dtype(d->dtype_in);
-    // A: [nA][M][K]; a padded copy when K*2 bytes is not a multiple of 16 or A is misaligned.
-    const void *ap = A;
-    int64_t lda = K;
-    if (((uintptr_t)A & 15) || (K * es) % 16) {
-      lda = round_up(K, 8);
-      if ((rc = sa.get(dev, st, (size_t)(nA * M * lda) * es))) return rc;
-      MPC_CUDA(dev, cudaMemcpy2DAsync(sa.ptr, lda * es, A, K * es, K * es, nA * M, cudaMemcpyDeviceToDevice, st));
-      ap = sa.ptr;
-    }
-    if ((rc = make_map_3d(&maps.a, dt, ap, K, M, nA, lda * es, M * lda * es, 64, 128, SW))) return rc;
-    const void *bp = B;
-    if (b_mn) {  // B [nB][K][N]
-      int64_t ldb = N;
-      if (((uintptr_t)B & 15) || (N * es) % 16) {
-        ldb = round_up(N, 8);
-        if ((rc = sb.get(dev, st, (size_t)(nB * K * ldb) * es))) return rc;
-        MPC_CUDA(dev, cudaMemcpy2DAsync(sb.ptr, ldb * es, B, N * es, N * es, nB * K, cudaMemcpyDeviceToDevice, st));
-        bp = sb.ptr;
-      }
-      if ((rc = make_map_3d(&maps.b, dt, bp, N, K, nB, ldb * es, K * ldb * es, 64, 64, SW))) return rc;
-      rc = launch<kHalf, true, 256, 4>(dev, maps, p, st);
-    } else {  // B [nB][N][K]
-      int64_t ldb = K;
-      if (((uintptr_t)B & 15) || (K * es) % 16) {
-        ldb = round_up(K, 8);
-        if ((rc = sb.get(dev, st, (size_t)(nB * N * ldb) * es))) return rc;
-        MPC_CUDA(dev, cudaMemcpy2DAsync(sb.ptr, ldb * es, B, K * es, K * es, nB * N, cudaMemcpyDeviceToDevice, st));
-        bp = sb.ptr;
-      }
-      if ((rc = make_map_3d(&maps.b, dt, bp, K, N, nB, ldb * es, N * ldb * es, 64, 256, SW))) return rc;
-      rc = launch<kHalf, false, 256, 4>(dev, maps, p, st);
-    }
-  }
+  else if (pr.b_mn)
+    rc = launch<kHalf, true, 256, 4>(dev, maps, p, st);
+  else
+    rc = launch<kHalf, false, 256, 4>(dev, maps, p, st);
   if (rc) return rc;
   if (cdst != Cout)
     MPC_CUDA(dev, cudaMemcpy2DAsync(Cout, N * eo, cdst, ldc * eo, N * eo, batch * M, cudaMemcpyDeviceToDevice, st));
   return MPC_OK;
+}
+
+// The product stored into several row-major matrices at once (row pitch ldc elements, columns
+// col_offset .. col_offset + N - 1 of each): the epilogue issues one TMA store per destination for
+// every output block. With the destinations being every rank's copy of a column-split result in
+// peer memory, this is a GEMM fused with its all-gather.
+int gemm_run_multi(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, const float *bias,
+                   void *const *dsts, int ndst, int64_t ldc, int64_t col_offset, cudaStream_t st) {
+  using namespace gemm;
+  const char *who = "mpc_gemm_multi_store";
+  if (ndst < 1 || ndst > kMaxDst) return fail(MPC_ERR_INVALID, "%s: %d destinations (1..%d)", who, ndst, kMaxDst);
+  if (!dsts) return fail(MPC_ERR_INVALID, "%s: null destination list", who);
+  Params p;
+  Prep pr;
+  int rc = prepare(dev, d, bias, who, p, pr);
+  if (rc) return rc;
+  if (pr.tf32) return fail(MPC_ERR_UNSUPPORTED, "%s: f16 / bf16 operands only", who);
+  const int64_t M = d->m, N = d->n, K = d->k, batch = pr.batch;
+  const size_t eo = dtype_size(d->dtype_out);
+  if (col_offset < 0 || ldc < col_offset + N)
+    return fail(MPC_ERR_INVALID, "%s: columns [%lld, %lld) do not fit rows of %lld", who, (long long)col_offset,
+                (long long)(col_offset + N), (long long)ldc);
+  if ((ldc * eo) % 16 || (col_offset * eo) % 16)
+    return fail(MPC_ERR_INVALID, "%s: row pitch and column offset must be multiples of 16 bytes", who);
+  for (int i = 0; i < ndst; ++i)
+    if (!dsts[i] || ((uintptr_t)dsts[i] & 15)) return fail(MPC_ERR_INVALID, "%s: destination %d null or misaligned", who, i);
+  if (batch == 0 || M == 0 || N == 0) return MPC_OK;
+  if (!A || !B) return fail(MPC_ERR_INVALID, "%s: null operand pointer", who);
+  if (K == 0) return fail(MPC_ERR_UNSUPPORTED, "%s: K == 0", who);
+  MapsT<kMaxDst> maps;
+  memset(&maps, 0, sizeof(maps));
+  for (int i = 0; i < ndst; ++i) {
+    void *base = static_cast<uint8_t *>(dsts[i]) + col_offset * eo;
+    if ((rc = make_map_3d(&maps.c[i], tmap_dtype(d->dtype_out), base, N, M, batch, ldc * eo, M * ldc * eo, 32, 32,
+                          eo == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
+      return rc;
+  }
+  p.ndst = ndst;
+  OperandScratch s;
+  if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st))) return rc;
+  if (pr.b_mn) return launch<kHalf, true, 256, 4, kMaxDst>(dev, maps, p, st);
+  return launch<kHalf, false, 256, 4, kMaxDst>(dev, maps, p, st);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -744,6 +837,7 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
   p.out_dtype = MPC_F32;
   p.err = dev->d_err;
   p.timeout_ns = dev->timeout_ns;
+  p.ndst = 1;
   split_rows_kernel<<<1184, 256, 0, st>>>(A, a_hi, a_lo, nA * M, K, ldk);
   if (d->b_layout == MPC_B_NK) {
     split_rows_kernel<<<1184, 256, 0, st>>>(B, b_hi, b_lo, nB * N, K, ldk);
@@ -761,7 +855,7 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
       (rc = make_map_3d(&maps.a_lo, f32, a_lo, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
       (rc = make_map_3d(&maps.b, f32, b_hi, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)) ||
       (rc = make_map_3d(&maps.b_lo, f32, b_lo, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)) ||
-      (rc = make_map_3d(&maps.c, f32, cdst, N, M, batch, ldc * 4, M * ldc * 4, 32, 32, SW)))
+      (rc = make_map_3d(&maps.c[0], f32, cdst, N, M, batch, ldc * 4, M * ldc * 4, 32, 32, SW)))
     return rc;
   if ((rc = launch<kTF32x3, false, 128, 3>(dev, maps, p, st))) return rc;
   if (stage_c)

@@ -41,6 +41,13 @@ struct mpc_device {
   mpc_allocator alloc;
 };
 
+// One rank of an NCCL communicator (comm.cu).
+struct mpc_comm {
+  mpc_device *dev;
+  void *comm;  // ncclComm_t
+  int nranks, rank;
+};
+
 namespace mpc {
 
 // Thread-local last-error text and the helpers that fill it.
@@ -111,5 +118,8 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
 int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void *K, const void *V, const void *mask,
              void *O, float *LSE, cudaStream_t st);
 int wait_probe_run(mpc_device *dev, uint64_t timeout_ns, cudaStream_t st);
+// The product stored into `ndst` row-major matrices (pitch ldc, columns col_offset..+N-1).
+int gemm_run_multi(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, const float *bias,
+                   void *const *dsts, int ndst, int64_t ldc, int64_t col_offset, cudaStream_t st);
 
 }  // namespace mpc

@@ -163,6 +163,31 @@ __global__ void cast_kernel(const void *__restrict__ x, int dti, void *__restric
     store_from_f32(out, dto, i, load_as_f32(x, dti, i));
 }
 
+// out = x permuted: out[i_0..i_{r-1}] = x[... i_k at axis perm[k] ...]. Each thread gathers one
+// element (or one 16-byte unit when the innermost axis is kept); writes are coalesced.
+struct PermParams {
+  int rank;
+  long long out_shape[6];
+  long long in_stride[6];  // element stride in x of output axis k (= x's stride of axis perm[k])
+  long long total;
+};
+template <typename T>
+__global__ void permute_kernel(const T *__restrict__ x, T *__restrict__ out, const PermParams p) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.total;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long rem = i, off = 0;
+#pragma unroll
+    for (int k = 5; k >= 0; --k) {
+      if (k < p.rank) {
+        const long long c = rem % p.out_shape[k];
+        rem /= p.out_shape[k];
+        off += c * p.in_stride[k];
+      }
+    }
+    out[i] = x[off];
+  }
+}
+
 bool float_dtype(int dt) { return dt == MPC_F32 || dt == MPC_F16 || dt == MPC_BF16; }
 
 unsigned grid_for(mpc_device *dev, int64_t n, int threads) {
@@ -272,6 +297,60 @@ int mpc_cast(mpc_device *dev, const void *x, int32_t dti, void *out, int32_t dto
   cast_kernel<<<grid_for(dev, n, 256), 256, 0, stream_of(dev, s)>>>(x, dti, out, dto, n);
   dev->launches++;
   return check_launch(dev, "cast_kernel");
+}
+
+int mpc_transpose(mpc_device *dev, const void *x, void *out, int32_t elem_bytes, int32_t rank, const int64_t *shape,
+                  const int32_t *perm, mpc_stream s) {
+  int rc = enter(dev);
+  if (rc) return rc;
+  if (rank < 1 || rank > 6 || !shape || !perm) return fail(MPC_ERR_INVALID, "mpc_transpose: rank %d (1..6)", rank);
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8)
+    return fail(MPC_ERR_INVALID, "mpc_transpose: element size %d", elem_bytes);
+  long long in_shape[6], in_stride[6], total = 1;
+  bool seen[6] = {false, false, false, false, false, false};
+  for (int k = 0; k < rank; ++k) {
+    if (shape[k] < 0) return fail(MPC_ERR_INVALID, "mpc_transpose: negative extent");
+    if (perm[k] < 0 || perm[k] >= rank || seen[perm[k]])
+      return fail(MPC_ERR_INVALID, "mpc_transpose: [%d...] is not a permutation", perm[0]);
+    seen[perm[k]] = true;
+    in_shape[k] = shape[k];
+    total *= shape[k];
+  }
+  if (total == 0) return MPC_OK;
+  if (!x || !out) return fail(MPC_ERR_INVALID, "mpc_transpose: null pointer");
+  long long acc = 1;
+  for (int k = rank - 1; k >= 0; --k) {
+    in_stride[k] = acc;
+    acc *= in_shape[k];
+  }
+  PermParams p{};
+  p.rank = rank;
+  p.total = total;
+  for (int k = 0; k < rank; ++k) {
+    p.out_shape[k] = in_shape[perm[k]];
+    p.in_stride[k] = in_stride[perm[k]];
+  }
+  // Innermost axis kept in place with 16-byte rows: move 16-byte units instead of elements.
+  int eb = elem_bytes;
+  if (perm[rank - 1] == rank - 1 && (in_shape[rank - 1] * elem_bytes) % 16 == 0 && !((uintptr_t)x & 15) &&
+      !((uintptr_t)out & 15)) {
+    const long long f = 16 / elem_bytes;
+    p.out_shape[rank - 1] /= f;
+    for (int k = 0; k < rank - 1; ++k) p.in_stride[k] /= f;
+    p.total /= f;
+    eb = 16;
+  }
+  cudaStream_t st = stream_of(dev, s);
+  const unsigned grid = grid_for(dev, p.total, 256);
+  switch (eb) {
+    case 1: permute_kernel<uint8_t><<<grid, 256, 0, st>>>((const uint8_t *)x, (uint8_t *)out, p); break;
+    case 2: permute_kernel<uint16_t><<<grid, 256, 0, st>>>((const uint16_t *)x, (uint16_t *)out, p); break;
+    case 4: permute_kernel<uint32_t><<<grid, 256, 0, st>>>((const uint32_t *)x, (uint32_t *)out, p); break;
+    case 8: permute_kernel<uint2><<<grid, 256, 0, st>>>((const uint2 *)x, (uint2 *)out, p); break;
+    default: permute_kernel<uint4><<<grid, 256, 0, st>>>((const uint4 *)x, (uint4 *)out, p); break;
+  }
+  dev->launches++;
+  return check_launch(dev, "permute_kernel");
 }
 
 }  // extern "C"

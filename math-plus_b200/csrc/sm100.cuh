@@ -19,6 +19,7 @@ enum : int {
   kErrWaitAccEmpty = 0x103,  // MMA warp waiting for the epilogue to drain a TMEM accumulator
   kErrWaitAccFull = 0x104,   // epilogue waiting for a finished accumulator
   kErrWaitSoftmax = 0x105,   // attention: waits between MMA and softmax warps
+  kErrWaitPeer = 0x106,      // peer barrier: a rank's signal did not arrive
   kErrWaitProbe = 0x1FF,     // the self-test wait that nothing releases
 };
 

@@ -98,11 +98,18 @@ SIGNATURES = {
     "mpc_layer_norm": [_dev, _vp, _i32, _vp, _vp, C.c_float, _vp, _i32, _i64, _i64, _vp],
     "mpc_embedding": [_dev, _vp, _i32, _vp, _vp, _i64, _i64, _i64, C.POINTER(_i64), _vp],
     "mpc_cast": [_dev, _vp, _i32, _vp, _i32, _i64, _vp],
+    "mpc_transpose": [_dev, _vp, _vp, _i32, _i32, C.POINTER(_i64), C.POINTER(_i32), _vp],
     "mpc_comm_unique_id": [_vp],
     "mpc_comm_init": [_dev, C.c_int, C.c_int, _vp, C.POINTER(_vp)],
     "mpc_comm_destroy": [_vp],
     "mpc_comm_abort": [_vp],
     "mpc_allgather": [_vp, _vp, _vp, _sz, _vp],
+    "mpc_peer_buffer_create": [_vp, _sz, C.POINTER(_vp)],
+    "mpc_peer_buffer_ptr": [_vp, C.c_int, C.POINTER(_vp)],
+    "mpc_peer_barrier": [_vp, _vp],
+    "mpc_peer_buffer_destroy": [_vp],
+    "mpc_gemm_multi_store": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, C.POINTER(_vp), _i32, _i64, _i64, _vp],
+    "mpc_gemm_allgather": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
 }
 _RESTYPE = {"mpc_last_error": C.c_char_p}
 

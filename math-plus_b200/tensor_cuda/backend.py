@@ -259,6 +259,22 @@ class CudaBackend:
         _ = x.ptr
         return self._make(shape, x.dtype, x._buf.retain())  # a view sharing the buffer
 
+    def transpose(self, x: CudaTensor, perm=None) -> CudaTensor:
+        """Axis permutation (default: reversed), like numpy.transpose (device-array.ts:457-471)."""
+        self._check_live(x)
+        nd = len(x.shape)
+        perm = list(range(nd - 1, -1, -1)) if perm is None else [p % nd if nd else p for p in perm]
+        if sorted(perm) != list(range(nd)):
+            raise ValueError(f"tensor-cuda: transpose: {perm} is not a permutation")
+        if nd <= 1 or perm == list(range(nd)):
+            return self.reshape(x, x.shape)
+        out = self._alloc(tuple(x.shape[p] for p in perm), x.dtype)
+        shape = (C.c_int64 * nd)(*x.shape)
+        pm = (C.c_int32 * nd)(*perm)
+        F.call("mpc_transpose", self.device.handle, C.c_void_p(x.ptr), C.c_void_p(out._buf.ptr),
+               F.DTYPE_BYTES[F.DTYPE_CODES[x.dtype]], nd, shape, pm, None)
+        return out
+
     def cast(self, x: CudaTensor, dtype: str) -> CudaTensor:
         self._check_live(x)
         if dtype == x.dtype:

@@ -241,6 +241,10 @@ class DeviceArray:
     def reshape(self, shape) -> "DeviceArray":
         return self._wrap(self.device.backend.reshape(self._handle("reshape"), shape))
 
+    def transpose(self, axes=None) -> "DeviceArray":
+        """Permute axes (default: reverse them), like numpy.transpose."""
+        return self._wrap(self.device.backend.transpose(self._handle("transpose"), axes))
+
 
 class CudaDevice(ArrayDevice):
     """The CUDA device facade (the shape of WebGpuDevice, packages/tensor-webgpu/src/facade.ts:93-199)."""

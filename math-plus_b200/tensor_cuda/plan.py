@@ -164,3 +164,39 @@ def batch_shard(batch: int, world: int, rank: int) -> tuple:
     """Contiguous batch shard (start, count) of rank ``rank``."""
     s, w = column_shards(batch, world)[rank]
     return s, w
+
+
+_ELEM_BYTES = {"f32": 4, "f16": 2, "bf16": 2}
+
+
+@dataclass(frozen=True)
+class ColumnSplitPlan:
+    m: int
+    n_total: int
+    k: int
+    world: int
+    n_shard: int
+    shards: tuple  # (first column, width) per rank
+
+    def gathered_to_output_perm(self) -> tuple:
+        """The permutation that turns the shard-major all-gather result [world, m, n_shard]
+        into row-major C [m, world, n_shard] = [m, n_total]."""
+        return (1, 0, 2)
+
+
+def column_split_plan(m: int, n_total: int, k: int, world: int, dtype_out: str = "bf16") -> ColumnSplitPlan:
+    """C [m, n_total] = A [m, k] @ B [k, n_total] with B's columns split evenly over ``world``
+    ranks. Every rank's column block must start on a 16-byte boundary of C's rows (the epilogue's
+    TMA stores and the all-gather blocks), so ``n_total / world`` elements must be a multiple of
+    16 bytes."""
+    if world < 1 or world > 8:
+        raise ValueError(f"column split over {world} ranks (1..8)")
+    if m <= 0 or n_total <= 0 or k <= 0:
+        raise ValueError(f"column split of a [{m},{k}] @ [{k},{n_total}] product")
+    if n_total % world:
+        raise ValueError(f"column split: {n_total} columns do not divide over {world} ranks")
+    n = n_total // world
+    eo = _ELEM_BYTES[dtype_out]
+    if (n * eo) % 16:
+        raise ValueError(f"column split: a {n}-column block of {dtype_out} is not a multiple of 16 bytes")
+    return ColumnSplitPlan(m, n_total, k, world, n, tuple(column_shards(n_total, world)))

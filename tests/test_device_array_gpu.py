@@ -176,3 +176,17 @@ def test_backend_sdpa_and_embedding(dev):
     assert emb.shape == (1, 3, 6)
     with pytest.raises(IndexError, match="out of range"):
         dev.backend.embedding(table.handle, dev.from_numpy(np.array([0, 5, 11], np.int32)).handle)
+
+
+def test_transpose_like_numpy(dev):
+    """device-array-suite.ts:178-179: transpose [2,3,4] -> [2,0,1] and the default reversal, every dtype."""
+    x = np.arange(24, dtype=np.float32).reshape(2, 3, 4)
+    for dtype, arr in (("f32", x), ("f16", x.astype(np.float16)), ("i32", x.astype(np.int32))):
+        a = dev.from_numpy(arr)
+        assert np.array_equal(run(a.transpose([2, 0, 1]).toTensor()), np.transpose(arr, [2, 0, 1])), dtype
+        assert np.array_equal(run(a.transpose().toTensor()), np.transpose(arr)), dtype
+    big = O.normal_f32(4 * 64 * 3 * 12 * 64, 3).reshape(4, 64, 3, 12, 64)  # a QKV head split
+    got = run(dev.from_numpy(big).transpose([2, 0, 3, 1, 4]).toTensor())
+    assert np.array_equal(got, np.transpose(big, [2, 0, 3, 1, 4]))
+    with pytest.raises(ValueError, match="permutation"):
+        dev.from_numpy(x).transpose([0, 0, 1])
