@@ -166,14 +166,20 @@ int mpc_peer_buffer_destroy(mpc_peer_buffer *b) {
   if (!b) return MPC_OK;
   int rc = enter(b->dev);
   if (rc) return rc;
-  // No rank may still write into an allocation that its owner frees: barrier, unmap, barrier, free.
+  // No rank may still write into an allocation that its owner frees, and no rank frees its
+  // allocation while another still maps it: a device barrier (all peer stores have landed), unmap
+  // the peers, then a barrier that touches only local memory (an NCCL all-gather of one byte per
+  // rank inside this rank's own signal area; the peer mappings are gone by then), then free.
   cudaStream_t st = b->dev->stream;
   int status = peer_barrier_launch(b, st);
   cudaError_t e = cudaStreamSynchronize(st);
   for (int r = 0; r < b->world; ++r)
     if (r != b->rank && b->base[r]) cudaIpcCloseMemHandle(b->base[r]);
-  if (!status) status = peer_barrier_launch(b, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  uint8_t *sig = b->base[b->rank] + data_span(b->bytes);
+  const int ag = mpc_allgather(b->comm, sig + 64, sig + 128, 1, st);
+  if (!status) status = ag;
+  const cudaError_t e2 = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = e2;
   cudaFree(b->base[b->rank]);
   delete b;
   if (status) return status;

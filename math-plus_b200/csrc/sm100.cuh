@@ -1,5 +1,5 @@
 // sm_100a building blocks shared by the GEMM and attention kernels: mbarriers with bounded
-// waits, TMA tensor copies (no cluster multicast anywhere), and the tcgen05 tensor-core /
+// waits, TMA tensor copies (plain per-CTA copies only), and the tcgen05 tensor-core /
 // tensor-memory instructions, as inline PTX.
 #pragma once
 
