@@ -18,8 +18,9 @@ A step is one pass of the hot path over one batch of synthetic input:
   nsplit_gemm_bf16             C[16384,65536] = A[16384,8192] @ B[8192,65536] bf16 -> bf16 with B's
                                columns split over the N ranks (strong scaling: the total work is
                                fixed); each rank's GEMM epilogue stores its blocks into every rank's
-                               copy of C over NVLink (the all-gather fused into the GEMM). The line
-                               also carries the GEMM-only and GEMM + NCCL all-gather + permute times.
+                               shard-major copy of C over NVLink (the all-gather fused into the
+                               GEMM), then a local permute to row-major. The line also carries the
+                               blocked-view-only, GEMM-only and GEMM + NCCL all-gather + permute times.
 
 ``value`` is device-timed throughput with inputs resident in HBM (CUDA events on the launching
 stream, barrier + synchronize around the timed region, max over ranks). ``e2e`` runs the same
@@ -252,7 +253,7 @@ def run_reference(args, w):
                                    "gemmNT / attention, OpenMP over row blocks / heads"},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -312,7 +313,7 @@ def setup_nsplit(w, dev, torch, g, local, F, world, pg):
     group = PeerGroup.from_torch(dev) if world > 1 else PeerGroup(dev, 0, 1, unique_id())
     fused = ColumnSplitGemm(group, M, n, K, "bf16", w["out"], F.B_KN, fused=True)
 
-    class Out:  # this rank's whole C, in the peer buffer
+    class Out:  # this rank's whole row-major C
         ptr = fused.out_ptr
         nbytes = M * w["n"] * F.DTYPE_BYTES[F.DTYPE_CODES[w["out"]]]
 
@@ -439,13 +440,19 @@ def run_ours(args, w):
         nccl = ColumnSplitGemm(extras["group"], w["m"], extras["pl"].n_shard, w["k"], "bf16", w["out"], F.B_KN,
                                fused=False)
         nccl_step = lambda: nccl(ptrs[0], ptrs[1], stream)
-        for fn in (gemm_only, nccl_step):
+        blocks = ColumnSplitGemm(extras["group"], w["m"], extras["pl"].n_shard, w["k"], "bf16", w["out"], F.B_KN,
+                                 fused=True, layout="blocks")
+        blocks_step = lambda: blocks(ptrs[0], ptrs[1], stream)
+        for fn in (gemm_only, nccl_step, blocks_step):
             for _ in range(max(1, args.warmup)):
                 fn()
         breakdown = {"fused_gemm_allgather": ms_step,
+                     "fused_gemm_allgather_blocked_layout": max_over_ranks(
+                         time_region(dev, stream, blocks_step, args.steps, barrier)),
                      "gemm_only": max_over_ranks(time_region(dev, stream, gemm_only, args.steps, barrier)),
                      "gemm_then_nccl_allgather_then_permute": max_over_ranks(
                          time_region(dev, stream, nccl_step, args.steps, barrier))}
+        blocks.destroy()
         nccl.destroy()
         local_c.free()
 
@@ -517,7 +524,8 @@ def run_ours(args, w):
                        "sample": sample + f" ({secs:.1f} s); the oracle's restatement of the reference's CPU path"}
             except Exception as ex:  # reported, never required
                 cpu = {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
-        par = (f"column split over {world} GPUs, all-gather fused into the GEMM epilogue (peer stores)" if strong
+        par = (f"column split over {world} GPUs, all-gather fused into the GEMM epilogue (peer stores into the "
+               "shard-major view), then a local permute to row-major" if strong
                else f"dp{world} (shards, no collective)")
         cfg = {"workload": args.workload, "description": w["desc"], "parallelism": par}
         if breakdown:
@@ -533,7 +541,7 @@ def run_ours(args, w):
             "config": cfg, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
             "clocks": clocks,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if extras:
         extras["fused"].destroy()
         extras["group"].destroy()
@@ -541,7 +549,22 @@ def run_ours(args, w):
         pg.destroy_process_group()
 
 
+_RESULT = None  # the stream the JSON line goes to (the process's original stdout)
+
+
+def emit(line: dict) -> None:
+    out = _RESULT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def main():
+    global _RESULT
+    # Libraries print to stdout on their own (NCCL's version banner, for one): send file
+    # descriptor 1 to stderr for the whole run and keep the original stdout for the one JSON line.
+    sys.stdout.flush()
+    _RESULT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     args = parse_args()
     w = dict(WORKLOADS[args.workload])
     if args.batch is not None:

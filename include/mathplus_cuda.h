@@ -223,12 +223,14 @@ int mpc_gemm_multi_store(mpc_device *dev, const mpc_gemm_desc *desc, const void 
                          const float *bias, void *const *dsts, int32_t ndst, int64_t ldc, int64_t col_offset,
                          mpc_stream s);
 /* Column-split GEMM with its all-gather in one kernel: rank r of p computes A [m, k] times its
- * column block B_r (desc->n = n columns) and the epilogue writes each output block into every
- * rank's C buffer, so that on return (in stream order) every rank's buffer holds the whole
- * row-major C [m, p*n], rank r's block at columns r*n .. r*n + n - 1. A peer barrier precedes
- * the GEMM (no rank still reads the previous C) and follows it (all blocks have landed). */
+ * column block B_r (desc->n = n columns, one matrix) and the epilogue writes each output block
+ * into every rank's C buffer, so that on return (in stream order) every rank's buffer holds the
+ * whole C as the shard-major blocked view [p, m, n] (rank r's block contiguous at index r). When
+ * rows_out is not null, a permute also writes the row-major C [m, p*n] there (local memory,
+ * m*p*n elements of desc->dtype_out). A peer barrier precedes the GEMM (no rank still reads the
+ * previous C) and follows it (all blocks have landed). */
 int mpc_gemm_allgather(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B,
-                       const float *bias, mpc_peer_buffer *C, mpc_stream s);
+                       const float *bias, mpc_peer_buffer *C, void *rows_out, mpc_stream s);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -10,7 +10,7 @@
 //               stage releases and accumulator completion to mbarriers; also owns the TMEM allocation
 //   warps 2..9  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes 32*(w%4)..+31; two
 //               warps per lane quadrant split the columns), apply alpha / +bias / exact-erf GELU,
-//               convert, stage 32-row x 32-column swizzled blocks in shared memory and TMA-store
+//               convert, stage 32-row x 128-byte swizzled blocks in shared memory and TMA-store
 //               them (bounds clipped by the tensor map)
 // Two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1.
 //
@@ -130,20 +130,19 @@ __device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], i
   }
 }
 
-// Writes row `lane` of a 32-row staging block in the layout the store map's swizzle expects:
-// f32 rows are 128 bytes (16-byte chunk j at chunk j ^ (row & 7), the 128-byte swizzle);
-// f16 / bf16 rows are 64 bytes (chunk j at j ^ ((row >> 1) & 3), the 64-byte swizzle).
-// Both orders are bank-conflict free for these 16-byte stores.
-__device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], int out_dtype, int lane) {
+// Writes row `lane` of a 32-row x 128-byte staging block in the 128-byte swizzle the store map
+// expects (16-byte chunk j of a row at chunk j ^ (row & 7); bank-conflict free). An f32 chunk of
+// 32 columns fills the row; a 16-bit chunk fills half of it (`half` selects which), so 16-bit
+// outputs go out as 32 x 64-column stores.
+__device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], int out_dtype, int lane, int half) {
+  uint8_t *row = buf + lane * 128;
   if (out_dtype == MPC_F32) {
-    uint8_t *row = buf + lane * 128;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
       *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) =
           make_uint4(__float_as_uint(f[4 * j]), __float_as_uint(f[4 * j + 1]), __float_as_uint(f[4 * j + 2]),
                      __float_as_uint(f[4 * j + 3]));
   } else {
-    uint8_t *row = buf + lane * 64;
     uint32_t w[16];
     if (out_dtype == MPC_BF16) {
 #pragma unroll
@@ -160,7 +159,7 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], in
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
-      *reinterpret_cast<uint4 *>(row + ((j ^ ((lane >> 1) & 3)) << 4)) =
+      *reinterpret_cast<uint4 *>(row + (((4 * half + j) ^ (lane & 7)) << 4)) =
           make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
   }
 }
@@ -358,18 +357,32 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
         }
         const int col0 = nt * BN + col_base + c * 32;
         epilogue_math(p, f, col0, lane);
-        if (lane == 0) tma_store_wait_read<0>();  // the previous store has finished reading the block
-        __syncwarp();
-        stage_row(buf, f, p.out_dtype, lane);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (row0 < p.M && col0 < p.N) {
-#pragma unroll
-            for (int d = 0; d < NDST; ++d)
-              if (d < p.ndst) tma_store_3d(&maps.c[d], buf, col0, row0, b);
+        // f32: one 32 x 32 store per chunk; 16-bit: chunks pair up into one 32 x 64 store
+        const bool wide = p.out_dtype != MPC_F32;
+        const int half = wide ? (c & 1) : 0;
+        if (half == 0) {
+          if (lane == 0) tma_store_wait_read<0>();  // the previous store has finished reading the block
+          __syncwarp();
+        }
+        stage_row(buf, f, p.out_dtype, lane, half);
+        if (!wide || half == 1) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int cs = col0 - 32 * half;
+            if (row0 < p.M && cs < p.N) {
+              if constexpr (NDST == 1) {
+                tma_store_3d(&maps.c[0], buf, cs, row0, b);
+              } else {  // the first destination rotates with the tile and warp: spread the peers' load
+                const int first = (tile + ew) % p.ndst;
+                for (int d = 0; d < p.ndst; ++d) {
+                  const int t = first + d < p.ndst ? first + d : first + d - p.ndst;
+                  tma_store_3d(&maps.c[t], buf, cs, row0, b);
+                }
+              }
+            }
+            tma_store_commit();
           }
-          tma_store_commit();
         }
       }
     }
@@ -653,8 +666,8 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
     if ((rc = sc.get(dev, st, (size_t)(batch * M * ldc) * eo))) return rc;
     cdst = sc.ptr;
   }
-  if ((rc = make_map_3d(&maps.c[0], tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo, 32, 32,
-                        eo == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
+  if ((rc = make_map_3d(&maps.c[0], tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo,
+                        128 / (uint32_t)eo, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st))) return rc;
   if (pr.tf32)
@@ -700,8 +713,8 @@ int gemm_run_multi(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const
   memset(&maps, 0, sizeof(maps));
   for (int i = 0; i < ndst; ++i) {
     void *base = static_cast<uint8_t *>(dsts[i]) + col_offset * eo;
-    if ((rc = make_map_3d(&maps.c[i], tmap_dtype(d->dtype_out), base, N, M, batch, ldc * eo, M * ldc * eo, 32, 32,
-                          eo == 4 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
+    if ((rc = make_map_3d(&maps.c[i], tmap_dtype(d->dtype_out), base, N, M, batch, ldc * eo, M * ldc * eo,
+                          128 / (uint32_t)eo, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
   }
   p.ndst = ndst;

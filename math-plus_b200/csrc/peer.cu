@@ -1,11 +1,11 @@
 // Peer memory over NVLink / NVSwitch and the GEMM fused with its all-gather.
 //
 // A column-split GEMM (rank r of p computes C[:, r*n : (r+1)*n] = A · B_r) needs every rank to end
-// up with the whole C. Instead of computing into a local shard and then running an all-gather and
-// a reassembly transpose, each rank's GEMM epilogue stores every finished output block straight
-// into every rank's copy of C, at the rank's column offset, through CUDA IPC mappings of the peers'
-// buffers. The NVLink transfer then overlaps the tensor-core work tile by tile, and C lands in its
-// final row-major layout.
+// up with the whole C. Instead of computing into a local shard and then running an all-gather,
+// each rank's GEMM epilogue stores every finished output block straight into every rank's copy of
+// C (the shard-major [p, m, n] view) through CUDA IPC mappings of the peers' buffers, so the
+// NVLink transfer overlaps the tensor-core work tile by tile. A local permute then gives the
+// row-major [m, p*n] where the caller asks for it.
 //
 // mpc_peer_buffer: one device allocation per rank (the data area plus a small signal area), its
 // IPC handle exchanged over the communicator, every peer's allocation opened in this process.
@@ -195,22 +195,31 @@ int mpc_gemm_multi_store(mpc_device *dev, const mpc_gemm_desc *desc, const void 
 }
 
 int mpc_gemm_allgather(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B, const float *bias,
-                       mpc_peer_buffer *C, mpc_stream s) {
+                       mpc_peer_buffer *C, void *rows_out, mpc_stream s) {
   int rc = enter(dev);
   if (rc) return rc;
   if (!desc || !C) return fail(MPC_ERR_INVALID, "mpc_gemm_allgather: null argument");
   if (C->dev != dev) return fail(MPC_ERR_INVALID, "mpc_gemm_allgather: the buffer belongs to another device");
   if (desc->batch_rank != 0) return fail(MPC_ERR_INVALID, "mpc_gemm_allgather: one matrix (batch_rank 0)");
-  const int64_t ldc = desc->n * C->world;
-  const size_t need = (size_t)(desc->m * ldc) * dtype_size(desc->dtype_out);
-  if (need > C->bytes)
-    return fail(MPC_ERR_INVALID, "mpc_gemm_allgather: C needs %zu bytes, the buffer has %zu", need, C->bytes);
+  const size_t eo = dtype_size(desc->dtype_out);
+  const size_t block = (size_t)(desc->m * desc->n) * eo;
+  if (block * C->world > C->bytes)
+    return fail(MPC_ERR_INVALID, "mpc_gemm_allgather: C needs %zu bytes, the buffer has %zu", block * C->world,
+                C->bytes);
   cudaStream_t st = stream_of(dev, s);
+  // Every rank's buffer is the shard-major [p, m, n]: this rank's block is the contiguous [m, n]
+  // at index rank in each of them. (Storing straight into a row-major [m, p*n] instead spreads
+  // every 128-row tile over 128 rows of p*n columns in p buffers at once; with 8 ranks that
+  // many distinct pages per tile made the peer stores an order of magnitude slower.)
   void *dsts[kMaxRanks];
-  for (int i = 0; i < C->world; ++i) dsts[i] = C->base[(C->rank + 1 + i) % C->world];  // own copy last
+  for (int i = 0; i < C->world; ++i) dsts[i] = C->base[(C->rank + 1 + i) % C->world] + block * C->rank;  // own last
   if ((rc = peer_barrier_launch(C, st))) return rc;  // every rank is done with the previous contents
-  if ((rc = gemm_run_multi(dev, desc, A, B, bias, dsts, C->world, ldc, desc->n * C->rank, st))) return rc;
-  return peer_barrier_launch(C, st);  // every rank's blocks have landed everywhere
+  if ((rc = gemm_run_multi(dev, desc, A, B, bias, dsts, C->world, desc->n, 0, st))) return rc;
+  if ((rc = peer_barrier_launch(C, st))) return rc;  // every rank's blocks have landed everywhere
+  if (!rows_out) return MPC_OK;
+  const int64_t shape[3] = {C->world, desc->m, desc->n};
+  const int32_t perm[3] = {1, 0, 2};  // [p, m, n] -> [m, p, n] = row-major [m, p*n]
+  return mpc_transpose(dev, C->base[C->rank], rows_out, (int32_t)eo, 3, shape, perm, s);
 }
 
 }  // extern "C"

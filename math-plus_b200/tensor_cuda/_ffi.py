@@ -109,7 +109,7 @@ SIGNATURES = {
     "mpc_peer_barrier": [_vp, _vp],
     "mpc_peer_buffer_destroy": [_vp],
     "mpc_gemm_multi_store": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, C.POINTER(_vp), _i32, _i64, _i64, _vp],
-    "mpc_gemm_allgather": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
+    "mpc_gemm_allgather": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp, _vp],
 }
 _RESTYPE = {"mpc_last_error": C.c_char_p}
 

@@ -5,9 +5,9 @@ it is split across GPUs: rank r of p computes ``C[:, r*n:(r+1)*n] = A @ B[:, r*n
 every rank ends up with the whole ``C [m, p*n]``. Two ways to get there:
 
 * ``ColumnSplitGemm(..., fused=True)`` (the default): one kernel per rank whose epilogue stores
-  each finished output block into every rank's copy of C through peer (IPC) mappings, so the
-  NVLink transfer overlaps the tensor-core work and C lands in its final row-major layout
-  (``mpc_gemm_allgather``);
+  each finished output block into every rank's copy of C (the shard-major ``[p, m, n]`` view)
+  through peer (IPC) mappings, so the NVLink transfer overlaps the tensor-core work; a local
+  permute gives the row-major ``[m, p*n]`` when asked for (``mpc_gemm_allgather``);
 * ``fused=False``: the GEMM into a local ``[m, n]`` shard, an NCCL all-gather into the
   shard-major ``[p, m, n]`` block, then a ``[p, m, n] -> [m, p, n]`` permute kernel.
 
@@ -96,47 +96,59 @@ class PeerBuffer:
 
 class ColumnSplitGemm:
     """``C = A @ B`` with B's columns split over the group: this rank holds ``A [m, k]`` and its
-    block ``B_r [k, n]`` (``b_layout=F.B_KN``) or ``[n, k]`` (``F.B_NK``); every rank gets
-    ``C [m, p*n]`` in ``self.out`` (a PeerBuffer when fused, else a local buffer)."""
+    block ``B_r [k, n]`` (``b_layout=F.B_KN``) or ``[n, k]`` (``F.B_NK``); every rank gets the whole
+    C, as row-major ``[m, p*n]`` (``layout="rows"``) or as the shard-major blocked view
+    ``[p, m, n]`` (``layout="blocks"``). ``__call__`` returns its device address."""
 
     def __init__(self, group: PeerGroup, m: int, n: int, k: int, dtype_in: str = "bf16", dtype_out: str = "bf16",
-                 b_layout: int = F.B_KN, fused: bool = True):
+                 b_layout: int = F.B_KN, fused: bool = True, layout: str = "rows"):
+        if layout not in ("rows", "blocks"):
+            raise ValueError(f"ColumnSplitGemm: layout {layout!r} (rows or blocks)")
         self.plan = P.column_split_plan(m, n * group.world, k, group.world, dtype_out)
-        self.group, self.m, self.n, self.k, self.fused = group, m, n, k, fused
+        self.group, self.m, self.n, self.k, self.fused, self.layout = group, m, n, k, fused, layout
         self.desc = gemm_desc(m, n, k, F.DTYPE_CODES[dtype_in], F.DTYPE_CODES[dtype_out], b_layout)
         self.eo = F.DTYPE_BYTES[F.DTYPE_CODES[dtype_out]]
         total = m * n * group.world * self.eo
         dev = group.device
+        # with one rank the blocked view [1, m, n] already is row-major
+        self.rows = dev.alloc(total) if layout == "rows" and group.world > 1 else None
         if fused:
-            self.out = group.peer_buffer(total)
-            self.out_ptr = self.out.ptr()
+            self.blocks = group.peer_buffer(total)
+            self.blocks_ptr = self.blocks.ptr()
         else:
             self.shard = dev.alloc(m * n * self.eo)
-            self.gathered = dev.alloc(total)
-            self.out = dev.alloc(total)
-            self.out_ptr = self.out.ptr
+            self.blocks = dev.alloc(total)
+            self.blocks_ptr = self.blocks.ptr
             self._shape = (C.c_int64 * 3)(group.world, m, n)
             self._perm = (C.c_int32 * 3)(*self.plan.gathered_to_output_perm())
 
+    @property
+    def out_ptr(self) -> int:
+        return self.rows.ptr if self.rows is not None else self.blocks_ptr
+
     def __call__(self, a: int, b: int, stream=None) -> int:
-        """Queues the step on ``stream``; returns the device address of this rank's full C."""
+        """Queues the step on ``stream``; returns the device address of this rank's whole C."""
         dev = self.group.device
+        rows = C.c_void_p(self.rows.ptr) if self.rows is not None else None
         if self.fused:
             F.call("mpc_gemm_allgather", dev.handle, C.byref(self.desc), C.c_void_p(a), C.c_void_p(b), None,
-                   self.out.handle, stream)
+                   self.blocks.handle, rows, stream)
             return self.out_ptr
         dev.gemm(self.desc, a, b, self.shard.ptr, None, stream)
-        self.group.allgather(self.shard.ptr, self.gathered.ptr, self.m * self.n * self.eo, stream)
-        F.call("mpc_transpose", dev.handle, C.c_void_p(self.gathered.ptr), C.c_void_p(self.out.ptr), self.eo, 3,
-               self._shape, self._perm, stream)
+        self.group.allgather(self.shard.ptr, self.blocks.ptr, self.m * self.n * self.eo, stream)
+        if rows is not None:
+            F.call("mpc_transpose", dev.handle, C.c_void_p(self.blocks.ptr), rows, self.eo, 3, self._shape,
+                   self._perm, stream)
         return self.out_ptr
 
     def destroy(self) -> None:
         if self.fused:
-            self.out.destroy()
+            self.blocks.destroy()
         else:
-            for b in (self.shard, self.gathered, self.out):
-                b.free()
+            self.shard.free()
+            self.blocks.free()
+        if self.rows is not None:
+            self.rows.free()
 
 
 def gemm_multi_store(device: Device, desc: F.GemmDesc, a: int, b: int, dsts, ldc: int, col_offset: int,

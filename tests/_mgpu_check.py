@@ -40,14 +40,21 @@ def main():
     da, db = dev.upload(a), dev.upload(mine)
     outs = {}
     for fused in (True, False):
-        cs = ColumnSplitGemm(group, m, n, k, "bf16", "bf16", F.B_KN, fused=fused)
-        for _ in range(3):
-            ptr = cs(da.ptr, db.ptr)
-        dev.sync()
-        raw = dev.download(ptr, m * n * world * 2, np.uint16, (m, n * world))
-        outs[fused] = from_device_dtype(raw, "bf16")
-        cs.destroy()
-    assert np.array_equal(outs[True], outs[False]), "fused and NCCL paths differ"
+        for layout in ("rows", "blocks"):
+            cs = ColumnSplitGemm(group, m, n, k, "bf16", "bf16", F.B_KN, fused=fused, layout=layout)
+            for _ in range(3):
+                ptr = cs(da.ptr, db.ptr)
+            dev.sync()
+            if layout == "rows":
+                raw = dev.download(ptr, m * n * world * 2, np.uint16, (m, n * world))
+            else:  # [p, m, n] -> [m, p, n]
+                raw = dev.download(ptr, m * n * world * 2, np.uint16, (world, m, n))
+                raw = np.ascontiguousarray(raw.transpose(1, 0, 2)).reshape(m, n * world)
+            outs[fused, layout] = from_device_dtype(raw, "bf16")
+            cs.destroy()
+    for key, c in outs.items():
+        assert np.array_equal(c, outs[True, "rows"]), f"{key} differs from the fused row-major result"
+    outs[True] = outs[True, "rows"]
     idx = rng.integers(0, [m, n * world], size=(512, 2))
     ref = np.array([np.dot(ea[i].astype(np.float64), eb[:, j].astype(np.float64)) for i, j in idx])
     got = outs[True][idx[:, 0], idx[:, 1]]

@@ -70,8 +70,8 @@ def test_multi_store_rejects_misaligned_offsets(dev):
         gemm_multi_store(dev, desc, a.ptr, a.ptr, [d.ptr] * 9, 64, 0)
 
 
-@pytest.mark.parametrize("fused", [True, False])
-def test_one_rank_column_split_equals_the_oracle(dev, fused):
+@pytest.mark.parametrize("fused,layout", [(True, "rows"), (False, "rows"), (True, "blocks"), (False, "blocks")])
+def test_one_rank_column_split_equals_the_oracle(dev, fused, layout):
     from tensor_cuda import _ffi as F
     from tensor_cuda.parallel import ColumnSplitGemm, PeerGroup, unique_id
     m, n, k = 256, 512, 320
@@ -79,7 +79,7 @@ def test_one_rank_column_split_equals_the_oracle(dev, fused):
     b, eb = to_device_dtype(O.lcg_gemm(k * n, 4).reshape(k, n), "bf16")
     g = PeerGroup(dev, 0, 1, unique_id())
     try:
-        cs = ColumnSplitGemm(g, m, n, k, "bf16", "f32", F.B_KN, fused=fused)
+        cs = ColumnSplitGemm(g, m, n, k, "bf16", "f32", F.B_KN, fused=fused, layout=layout)
         da, db = dev.upload(a), dev.upload(b)
         for _ in range(2):  # the second call reuses the buffers and barriers
             ptr = cs(da.ptr, db.ptr)
