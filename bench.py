@@ -56,6 +56,10 @@ WORKLOADS = {
                              epilogue="none", metric="GEMM TFLOP/s (column-split bf16 GEMM + all-gather)",
                              desc="C[16384,65536] = A[16384,8192] @ B[8192,65536] bf16, B's columns split over "
                                   "the ranks, every rank ends with the whole C (GEMM fused with its all-gather)"),
+    "gpt2_forward_bf16": dict(kind="gpt2", batch=32, seq=1024, dtype="bf16",
+                              metric="GPT-2-small forward TFLOP/s (bf16)",
+                              desc="GPT-2-small-shaped forward (12 layers, d 768, 12 heads, d_ff 3072, vocab 50257), "
+                                   "batch 32 x 1024 tokens, random-init bf16 weights ~ N(0, 0.02), logits bf16"),
     "causal_attention_f16": dict(kind="attention", batch=16, heads=32, seq=2048, head_dim=128, dtype="f16",
                                  causal=True, metric="fused attention TFLOP/s (causal f16)",
                                  desc="causal sdpa f16 [16,32,2048,128], scale 1/sqrt(128), f16 out + f32 LSE"),
@@ -164,6 +168,10 @@ def dist_env():
 
 
 def flop_per_step(w):
+    if w["kind"] == "gpt2":
+        sys.path.insert(0, os.path.join(ROOT, "math-plus_b200"))
+        from tensor_cuda.gpt2 import GPT2Config
+        return GPT2Config().forward_flop(w["batch"], w["seq"])
     if w["kind"] in ("gemm", "nsplit"):
         return 2.0 * w["batch"] * w["m"] * w["n"] * w["k"]
     f = 4.0 * w["batch"] * w["heads"] * w["seq"] * w["seq"] * w["head_dim"]
@@ -180,6 +188,25 @@ def cpu_sample_rate(w: dict, target_s: float, threads: int):
     import numpy as np
     import oracle as O
     rng = np.random.default_rng(7)
+    if w["kind"] == "gpt2":
+        sys.path.insert(0, os.path.join(ROOT, "math-plus_b200"))
+        from tensor_cuda.gpt2 import GPT2Config, random_weights
+        full = GPT2Config()
+        wts = random_weights(GPT2Config(n_layer=1), seed=3)
+        f = {k: ((v.astype(np.uint32) << 16).view(np.float32).reshape(v.shape) if v.dtype == np.uint16 else v)
+             for k, v in wts.items()}
+        L = 64
+        while True:
+            ids = rng.integers(0, full.vocab, (1, L), dtype=np.int32)
+            t0 = time.perf_counter()
+            O.gpt2_forward(f, ids, 1, full.n_head, full.eps, threads=threads)
+            dt = time.perf_counter() - t0
+            if dt >= target_s / 4 or L >= w["seq"]:
+                break
+            L = min(w["seq"], L * 2)
+        flop = GPT2Config(n_layer=1).forward_flop(1, L)
+        return flop / dt, (f"a 1-layer full-width forward (embedding, block, LN, LM head over the 50257-token "
+                           f"vocabulary) of one {L}-token sequence, f64 accumulate"), dt
     if w["kind"] == "attention":
         L, D = w["seq"], w["head_dim"]
         mask = np.tril(np.ones((L, L), np.bool_)).reshape(1, 1, L, L) if w["causal"] else None
@@ -325,6 +352,36 @@ def setup_nsplit(w, dev, torch, g, local, F, world, pg):
     return [A, Bs], Out, launch, "gemm_kernel<kHalf, B MN-major, BN=256, 4 stages, 8 output maps>", extras
 
 
+def setup_gpt2(w, dev, torch, g, local, F, rank):
+    import numpy as np
+
+    from tensor_cuda.backend import CudaBackend
+    from tensor_cuda.gpt2 import GPT2, GPT2Config, random_weights
+    cfg = GPT2Config()
+    be = CudaBackend(dev)
+    model = GPT2(be, cfg, random_weights(cfg, seed=1234))  # replicated weights
+    B, L = w["batch"], w["seq"]
+    ids = torch.randint(0, cfg.vocab, (B, L), generator=g, device=f"cuda:{local}", dtype=torch.int32)
+    state = {}
+
+    class Out:  # the last step's logits
+        nbytes = B * L * cfg.vocab * 2
+
+        @property
+        def ptr(self):
+            t = state.get("logits")
+            return t.ptr if t is not None else 0
+
+    def launch(ptrs, optr, stream):
+        if "logits" in state:
+            be.dispose(state.pop("logits"))
+        state["logits"] = model.forward(be.external(ptrs[0], (B, L), "i32"))
+        _ = state["logits"].ptr  # run the pending LM-head GEMM
+
+    return [ids], Out(), launch, "whole forward: 12 x (LN, QKV GEMM, head split, causal attention, head merge, " \
+        "out-proj GEMM, residual add, LN, fc GEMM + GELU, proj GEMM, residual add), LN, LM-head GEMM"
+
+
 def time_region(dev, stream, fn, steps, barrier):
     barrier()
     dev.stream_sync(stream)
@@ -367,6 +424,8 @@ def run_ours(args, w):
     if w["kind"] == "nsplit":
         g.manual_seed(1234)  # A is the same on every rank
         ins, out, launch, kernel_name, extras = setup_nsplit(w, dev, torch, g, local, F, world, pg)
+    elif w["kind"] == "gpt2":
+        ins, out, launch, kernel_name = setup_gpt2(w, dev, torch, g, local, F, rank)
     else:
         setup = setup_gemm if w["kind"] == "gemm" else setup_attention
         ins, out, launch, kernel_name = setup(w, dev, torch, g, local, F)

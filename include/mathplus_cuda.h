@@ -83,7 +83,11 @@ int mpc_device_clear_error(mpc_device *dev);
  * usable; clear it with mpc_device_clear_error). No fault, trap or hang is involved. */
 int mpc_selftest_wait_timeout(mpc_device *dev, uint64_t timeout_ns);
 
-/* ---- memory: a caching allocator per device (Backend.fromHost's one copy, index.ts:225) */
+/* ---- memory: a caching allocator per device (Backend.fromHost's one copy, index.ts:225) ----
+ * Stream-ordered like the library's kernels: mpc_free returns a block at the current point of the
+ * device stream, and mpc_alloc may hand it out again at once, for work queued on the device stream
+ * after that point. Work that uses a block on another stream must first wait for the device
+ * stream (an event recorded there). */
 int mpc_alloc(mpc_device *dev, size_t bytes, void **ptr);
 int mpc_free(mpc_device *dev, void *ptr);
 /* Cap on bytes handed out by mpc_alloc (0 = no cap): lets tests inject allocation failure. */
@@ -118,7 +122,7 @@ int mpc_launch_count(mpc_device *dev, uint64_t *count);
  * DeviceArray chain matmul -> add(bias) -> gelu fused into one kernel.
  * f16 / bf16 inputs run on tcgen05 (f32 accumulation); f32 inputs run 3xTF32 on tcgen05.
  * A is [batch.., M, K] and C is [batch, M, N], both row-major; bias is f32 [N]. */
-enum { MPC_EPI_BIAS = 1, MPC_EPI_GELU = 2 };
+enum { MPC_EPI_BIAS = 1, MPC_EPI_GELU = 2, MPC_EPI_RESIDUAL = 4 };
 enum { MPC_B_KN = 0, MPC_B_NK = 1 };
 typedef struct {
   int64_t m, n, k;
@@ -134,6 +138,11 @@ typedef struct {
 } mpc_gemm_desc;
 int mpc_gemm(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B, void *C,
              const float *bias, mpc_stream s);
+/* mpc_gemm with MPC_EPI_RESIDUAL: C = act(alpha * A·B + bias) + R, R [batch, M, N] contiguous in
+ * C's dtype (the residual add of a transformer block, DeviceArray.add after linear, fused into
+ * the GEMM's epilogue). R may be C itself (in-place accumulate). */
+int mpc_gemm_residual(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B, void *C,
+                      const float *bias, const void *R, mpc_stream s);
 
 /* Allocation-free variant of the f32 (3xTF32) path of mpc_gemm. It has no counterpart in the
  * reference: it exists for callers that cannot allocate device memory (code running during

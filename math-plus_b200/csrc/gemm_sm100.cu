@@ -50,7 +50,9 @@ struct Params {
   uint32_t idesc;  // tcgen05 instruction descriptor (operand format, B major, M, N)
   int *err;
   unsigned long long timeout_ns;
-  int ndst;  // output maps in use (1 unless the product is stored to several matrices)
+  int ndst;            // output maps in use (1 unless the product is stored to several matrices)
+  const void *resid;   // MPC_EPI_RESIDUAL: [batch, M, N] in the output type, added last
+  int resid_vec;       // resid rows start 16-byte aligned (vector loads)
 };
 
 // The operand maps and NDST output maps; each 32 x 32 output block is stored through c[0..ndst).
@@ -127,6 +129,49 @@ __device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], i
   if (p.epilogue & MPC_EPI_GELU) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) f[j] = gelu_erf_f32(f[j]);
+  }
+}
+
+// + R[b, row, col0 .. col0+31] (the residual, in the output type) for the lane's row.
+__device__ __forceinline__ void add_residual(const Params &p, float (&f)[32], int b, int row, int col0) {
+  if (row >= p.M) return;
+  const int64_t base = ((int64_t)b * p.M + row) * p.N + col0;
+  const int ncol = p.N - col0;
+  if (p.out_dtype == MPC_F32) {
+    const float *r = static_cast<const float *>(p.resid) + base;
+    if (ncol >= 32 && p.resid_vec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 v = reinterpret_cast<const float4 *>(r)[j];
+        f[4 * j] += v.x, f[4 * j + 1] += v.y, f[4 * j + 2] += v.z, f[4 * j + 3] += v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncol) f[j] += r[j];
+    }
+    return;
+  }
+  const uint16_t *r = static_cast<const uint16_t *>(p.resid) + base;
+  const bool bf = p.out_dtype == MPC_BF16;
+  auto widen = [bf](uint32_t h) {
+    return bf ? __uint_as_float(h << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+  };
+  if (ncol >= 32 && p.resid_vec) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 v = reinterpret_cast<const uint4 *>(r)[j];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        f[8 * j + 2 * e] += widen(w[e] & 0xFFFFu);
+        f[8 * j + 2 * e + 1] += widen(w[e] >> 16);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncol) f[j] += widen(r[j]);
   }
 }
 
@@ -357,6 +402,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
         }
         const int col0 = nt * BN + col_base + c * 32;
         epilogue_math(p, f, col0, lane);
+        if (p.epilogue & MPC_EPI_RESIDUAL) add_residual(p, f, b, row0 + lane, col0);
         // f32: one 32 x 32 store per chunk; 16-bit: chunks pair up into one 32 x 64 store
         const bool wide = p.out_dtype != MPC_F32;
         const int half = wide ? (c & 1) : 0;
@@ -556,7 +602,7 @@ static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, c
   p.group_m = 16;
   p.alpha = d->alpha;
   p.bias = bias;
-  p.epilogue = d->epilogue & (MPC_EPI_BIAS | MPC_EPI_GELU);
+  p.epilogue = d->epilogue & (MPC_EPI_BIAS | MPC_EPI_GELU | MPC_EPI_RESIDUAL);
   p.idesc = make_idesc(pr.tf32 ? kFmtTF32 : (d->dtype_in == MPC_BF16 ? kFmtBF16 : kFmtF16), pr.b_mn, 128, pr.BN);
   p.out_dtype = d->dtype_out;
   p.err = dev->d_err;
@@ -639,16 +685,22 @@ static int operand_maps(mpc_device *dev, const mpc_gemm_desc *d, const Prep &pr,
 }  // namespace gemm
 
 int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, void *Cout, const float *bias,
-             cudaStream_t st) {
+             const void *resid, cudaStream_t st) {
   using namespace gemm;
   Params p;
   Prep pr;
   int rc = prepare(dev, d, bias, "mpc_gemm", p, pr);
   if (rc) return rc;
   const int64_t M = d->m, N = d->n, K = d->k, batch = pr.batch;
+  if ((d->epilogue & MPC_EPI_RESIDUAL) && !resid)
+    return fail(MPC_ERR_INVALID, "mpc_gemm: RESIDUAL epilogue without a residual matrix");
   if (batch == 0 || M == 0 || N == 0) return MPC_OK;
   if (!A || !B || !Cout) return fail(MPC_ERR_INVALID, "mpc_gemm: null operand pointer");
   const size_t eo = dtype_size(d->dtype_out);
+  p.resid = (d->epilogue & MPC_EPI_RESIDUAL) ? resid : nullptr;
+  p.resid_vec = p.resid && !((uintptr_t)resid & 15) && (N * eo) % 16 == 0;
+  if (K == 0 && p.resid)
+    return fail(MPC_ERR_UNSUPPORTED, "mpc_gemm: RESIDUAL epilogue with K == 0");
   if (K == 0) {
     gemm::fill_epilogue_kernel<<<1184, 256, 0, st>>>(Cout, d->dtype_out, batch * M, N, bias, d->epilogue);
     dev->launches++;
@@ -697,6 +749,7 @@ int gemm_run_multi(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const
   int rc = prepare(dev, d, bias, who, p, pr);
   if (rc) return rc;
   if (pr.tf32) return fail(MPC_ERR_UNSUPPORTED, "%s: f16 / bf16 operands only", who);
+  if (d->epilogue & MPC_EPI_RESIDUAL) return fail(MPC_ERR_UNSUPPORTED, "%s: no RESIDUAL epilogue", who);
   const int64_t M = d->m, N = d->n, K = d->k, batch = pr.batch;
   const size_t eo = dtype_size(d->dtype_out);
   if (col_offset < 0 || ldc < col_offset + N)
@@ -845,6 +898,8 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
   p.group_m = 16;
   p.alpha = d->alpha;
   p.bias = bias;
+  if (d->epilogue & MPC_EPI_RESIDUAL)
+    return fail(MPC_ERR_UNSUPPORTED, "mpc_gemm_f32_noalloc: no RESIDUAL epilogue");
   p.epilogue = d->epilogue & (MPC_EPI_BIAS | MPC_EPI_GELU);
   p.idesc = make_idesc(kFmtTF32, false, 128, 128);
   p.out_dtype = MPC_F32;

@@ -19,13 +19,20 @@ struct mpc_block {
   size_t bytes;
 };
 
-// Caching device allocator: freed blocks are kept per rounded size and handed out again.
-// Every kernel of a device runs in stream order on the stream it was given; a freed block
-// records an event on the device stream so a request from another stream never reuses memory
-// that pending work may still touch.
+// A cached block: freed on `stream`, where `ev` was recorded at the time of the free.
+struct mpc_free_block {
+  void *ptr;
+  cudaEvent_t ev;
+  cudaStream_t stream;
+};
+
+// Caching device allocator: freed blocks are kept per rounded size and handed out again,
+// stream-ordered: a block freed on stream S is handed at once to a request for use on S (work
+// queued on S after the free runs after every earlier use), and to a request for another stream
+// only once the event recorded at the free has completed.
 struct mpc_allocator {
   std::mutex mu;
-  std::unordered_multimap<size_t, std::pair<void *, cudaEvent_t>> free_blocks;
+  std::unordered_multimap<size_t, mpc_free_block> free_blocks;
   std::unordered_map<void *, size_t> live;
   size_t in_use = 0, cached = 0, limit = 0;
 };
@@ -68,6 +75,8 @@ int check_launch(mpc_device *dev, const char *what);
 
 // Returns a block to the device cache once the work queued on `st` so far has finished.
 int free_on(mpc_device *dev, void *ptr, cudaStream_t st);
+// A block for work queued on `st` (stream-ordered reuse, see mpc_allocator).
+int alloc_on(mpc_device *dev, size_t bytes, cudaStream_t st, void **ptr);
 
 // Scratch memory from the device allocator for the kernels queued on one stream; the block is
 // handed back on scope exit, ordered after that stream's pending work.
@@ -84,7 +93,7 @@ struct Scratch {
   int get(mpc_device *d, cudaStream_t s, size_t bytes) {
     dev = d;
     st = s;
-    return mpc_alloc(d, bytes ? bytes : 256, &ptr);
+    return alloc_on(d, bytes ? bytes : 256, s, &ptr);
   }
 };
 
@@ -114,7 +123,7 @@ inline size_t dtype_size(int dt) {
 
 // Kernel entry points implemented in other translation units.
 int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, void *C, const float *bias,
-             cudaStream_t st);
+             const void *resid, cudaStream_t st);
 int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void *K, const void *V, const void *mask,
              void *O, float *LSE, cudaStream_t st);
 int wait_probe_run(mpc_device *dev, uint64_t timeout_ns, cudaStream_t st);

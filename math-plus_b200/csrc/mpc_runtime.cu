@@ -82,8 +82,9 @@ int free_on(mpc_device *dev, void *ptr, cudaStream_t st) {
   a.live.erase(it);
   a.in_use -= bytes;
   cudaEvent_t ev = nullptr;
-  if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess) cudaEventRecord(ev, st ? st : dev->stream);
-  a.free_blocks.emplace(bytes, std::make_pair(ptr, ev));
+  cudaStream_t on = st ? st : dev->stream;
+  if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess) cudaEventRecord(ev, on);
+  a.free_blocks.emplace(bytes, mpc_free_block{ptr, ev, on});
   a.cached += bytes;
   return MPC_OK;
 }
@@ -139,6 +140,55 @@ int wait_probe_run(mpc_device *dev, uint64_t timeout_ns, cudaStream_t st) {
   wait_probe_kernel<<<1, 32, 0, st>>>(dev->d_err, timeout_ns);
   dev->launches++;
   return check_launch(dev, "wait_probe_kernel");
+}
+
+// Size classes: 512-byte steps up to 1 MiB, then 2 MiB steps.
+static size_t round_alloc(size_t bytes) {
+  if (bytes <= 512) return 512;
+  if (bytes <= (1u << 20)) return (bytes + 511) & ~size_t(511);
+  return (bytes + (2u << 20) - 1) & ~size_t((2u << 20) - 1);
+}
+
+int alloc_on(mpc_device *dev, size_t bytes, cudaStream_t st, void **ptr) {
+  *ptr = nullptr;
+  const size_t sz = round_alloc(bytes);
+  mpc_allocator &a = dev->alloc;
+  std::lock_guard<std::mutex> lk(a.mu);
+  if (a.limit && a.in_use + sz > a.limit)
+    return fail(MPC_ERR_OOM, "mpc_alloc: %zu bytes would exceed the allocator cap (%zu in use of %zu)", sz, a.in_use,
+                a.limit);
+  auto range = a.free_blocks.equal_range(sz);
+  for (auto it = range.first; it != range.second; ++it) {
+    const mpc_free_block fb = it->second;
+    if (fb.stream != st && fb.ev && cudaEventQuery(fb.ev) != cudaSuccess) continue;  // another stream may still use it
+    cudaGetLastError();
+    if (fb.ev) cudaEventDestroy(fb.ev);
+    a.free_blocks.erase(it);
+    a.cached -= sz;
+    a.live[fb.ptr] = sz;
+    a.in_use += sz;
+    *ptr = fb.ptr;
+    return MPC_OK;
+  }
+  void *p = nullptr;
+  cudaError_t e = cudaMalloc(&p, sz);
+  if (e == cudaErrorMemoryAllocation && !a.free_blocks.empty()) {
+    // Release the cache (after the device drains) and retry once.
+    cudaGetLastError();
+    cudaDeviceSynchronize();
+    for (auto &kv : a.free_blocks) {
+      if (kv.second.ev) cudaEventDestroy(kv.second.ev);
+      cudaFree(kv.second.ptr);
+    }
+    a.free_blocks.clear();
+    a.cached = 0;
+    e = cudaMalloc(&p, sz);
+  }
+  if (e != cudaSuccess) return cuda_fail(dev, e, "cudaMalloc");
+  a.live[p] = sz;
+  a.in_use += sz;
+  *ptr = p;
+  return MPC_OK;
 }
 
 }  // namespace mpc
@@ -206,8 +256,8 @@ int mpc_device_destroy(mpc_device *dev) {
   {
     std::lock_guard<std::mutex> lk(dev->alloc.mu);
     for (auto &kv : dev->alloc.free_blocks) {
-      if (kv.second.second) cudaEventDestroy(kv.second.second);
-      cudaFree(kv.second.first);
+      if (kv.second.ev) cudaEventDestroy(kv.second.ev);
+      cudaFree(kv.second.ptr);
     }
     for (auto &kv : dev->alloc.live) cudaFree(kv.first);
   }
@@ -244,56 +294,12 @@ int mpc_set_wait_timeout_ns(mpc_device *dev, uint64_t ns) {
 }
 
 // ---- allocator ------------------------------------------------------------------------------
-static size_t round_alloc(size_t bytes) {
-  if (bytes <= 512) return 512;
-  if (bytes <= (1u << 20)) return (bytes + 511) & ~size_t(511);
-  return (bytes + (2u << 20) - 1) & ~size_t((2u << 20) - 1);
-}
-
 int mpc_alloc(mpc_device *dev, size_t bytes, void **ptr) {
   int rc = enter(dev);
   if (rc) return rc;
   if (!ptr) return fail(MPC_ERR_INVALID, "mpc_alloc: null out pointer");
   *ptr = nullptr;
-  const size_t sz = round_alloc(bytes);
-  mpc_allocator &a = dev->alloc;
-  std::lock_guard<std::mutex> lk(a.mu);
-  if (a.limit && a.in_use + sz > a.limit)
-    return fail(MPC_ERR_OOM, "mpc_alloc: %zu bytes would exceed the allocator cap (%zu in use of %zu)", sz, a.in_use,
-                a.limit);
-  auto range = a.free_blocks.equal_range(sz);
-  for (auto it = range.first; it != range.second; ++it) {
-    cudaEvent_t ev = it->second.second;
-    if (ev && cudaEventQuery(ev) != cudaSuccess) continue;  // pending work may still use it
-    cudaGetLastError();
-    void *p = it->second.first;
-    if (ev) cudaEventDestroy(ev);
-    a.free_blocks.erase(it);
-    a.cached -= sz;
-    a.live[p] = sz;
-    a.in_use += sz;
-    *ptr = p;
-    return MPC_OK;
-  }
-  void *p = nullptr;
-  cudaError_t e = cudaMalloc(&p, sz);
-  if (e == cudaErrorMemoryAllocation && !a.free_blocks.empty()) {
-    // Release the cache (after the device drains) and retry once.
-    cudaGetLastError();
-    cudaDeviceSynchronize();
-    for (auto &kv : a.free_blocks) {
-      if (kv.second.second) cudaEventDestroy(kv.second.second);
-      cudaFree(kv.second.first);
-    }
-    a.free_blocks.clear();
-    a.cached = 0;
-    e = cudaMalloc(&p, sz);
-  }
-  if (e != cudaSuccess) return cuda_fail(dev, e, "cudaMalloc");
-  a.live[p] = sz;
-  a.in_use += sz;
-  *ptr = p;
-  return MPC_OK;
+  return alloc_on(dev, bytes, dev->stream, ptr);
 }
 
 int mpc_free(mpc_device *dev, void *ptr) {
@@ -323,10 +329,10 @@ int mpc_trim(mpc_device *dev) {
   if (rc) return rc;
   std::lock_guard<std::mutex> lk(dev->alloc.mu);
   for (auto it = dev->alloc.free_blocks.begin(); it != dev->alloc.free_blocks.end();) {
-    cudaEvent_t ev = it->second.second;
+    cudaEvent_t ev = it->second.ev;
     if (ev) cudaEventSynchronize(ev);
     if (ev) cudaEventDestroy(ev);
-    cudaFree(it->second.first);
+    cudaFree(it->second.ptr);
     dev->alloc.cached -= it->first;
     it = dev->alloc.free_blocks.erase(it);
   }
@@ -488,7 +494,17 @@ int mpc_gemm(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const vo
   int rc = enter(dev);
   if (rc) return rc;
   if (!desc) return fail(MPC_ERR_INVALID, "mpc_gemm: null descriptor");
-  return gemm_run(dev, desc, A, B, C, bias, stream_of(dev, s));
+  if (desc->epilogue & MPC_EPI_RESIDUAL)
+    return fail(MPC_ERR_INVALID, "mpc_gemm: the RESIDUAL epilogue needs mpc_gemm_residual");
+  return gemm_run(dev, desc, A, B, C, bias, nullptr, stream_of(dev, s));
+}
+
+int mpc_gemm_residual(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B, void *C,
+                      const float *bias, const void *R, mpc_stream s) {
+  int rc = enter(dev);
+  if (rc) return rc;
+  if (!desc) return fail(MPC_ERR_INVALID, "mpc_gemm_residual: null descriptor");
+  return gemm_run(dev, desc, A, B, C, bias, R, stream_of(dev, s));
 }
 
 int mpc_sdpa(mpc_device *dev, const mpc_sdpa_desc *desc, const void *Q, const void *K, const void *V,

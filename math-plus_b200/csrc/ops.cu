@@ -94,6 +94,132 @@ __global__ void add_kernel(const void *__restrict__ x, const void *__restrict__ 
     store_from_f32(out, dt, i, load_as_f32(x, dt, i) + load_as_f32(y, dt, i % ny));
 }
 
+// ---- 16-byte vector forms for contiguous, aligned operands -----------------------------------
+// A uint4 holds 8 f16 / bf16 or 4 f32 values; conversion to f32 and back (RNE) per element.
+template <typename T>
+struct Vec;
+template <>
+struct Vec<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const uint4 &u, float *f) {
+    f[0] = __uint_as_float(u.x), f[1] = __uint_as_float(u.y), f[2] = __uint_as_float(u.z), f[3] = __uint_as_float(u.w);
+  }
+  __device__ static uint4 store(const float *f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+};
+template <>
+struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+  __device__ static void load(const uint4 &u, float *f) {
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __bfloat1622float2(h[i]);
+      f[2 * i] = t.x, f[2 * i + 1] = t.y;
+    }
+  }
+  __device__ static uint4 store(const float *f) {
+    uint4 u;
+    __nv_bfloat162 *h = reinterpret_cast<__nv_bfloat162 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    return u;
+  }
+};
+template <>
+struct Vec<__half> {
+  static constexpr int N = 8;
+  __device__ static void load(const uint4 &u, float *f) {
+    const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(h[i]);
+      f[2 * i] = t.x, f[2 * i + 1] = t.y;
+    }
+  }
+  __device__ static uint4 store(const float *f) {
+    uint4 u;
+    __half2 *h = reinterpret_cast<__half2 *>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    return u;
+  }
+};
+
+// out = x + y (y a repeated block of nyv vectors), 16-byte vectors.
+template <typename T>
+__global__ void add_vec_kernel(const uint4 *__restrict__ x, const uint4 *__restrict__ y, uint4 *__restrict__ out,
+                               int64_t nv, int64_t nyv) {
+  constexpr int N = Vec<T>::N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    float a[N], b[N];
+    Vec<T>::load(x[i], a);
+    Vec<T>::load(y[nyv == nv ? i : i % nyv], b);
+#pragma unroll
+    for (int j = 0; j < N; ++j) a[j] += b[j];
+    out[i] = Vec<T>::store(a);
+  }
+}
+
+// LayerNorm, one warp per row held in registers (one read, one write): rows of d elements, d a
+// multiple of the vector width and at most 32 * MAXV vectors. Two-pass mean / population
+// variance in f32 from the registers.
+template <typename T, int MAXV>
+__global__ void layer_norm_warp_kernel(const uint4 *__restrict__ x, const float *__restrict__ w,
+                                       const float *__restrict__ b, float eps, uint4 *__restrict__ out, int64_t rows,
+                                       int d) {
+  constexpr int N = Vec<T>::N;
+  const int dv = d / N;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
+    const uint4 *xr = x + r * dv;
+    float v[MAXV][N];
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k) {
+      const int j = lane + 32 * k;
+      if (j < dv) {
+        Vec<T>::load(xr[j], v[k]);
+#pragma unroll
+        for (int e = 0; e < N; ++e) s += v[k][e];
+      }
+    }
+    const float mean = warp_sum(s) / (float)d;
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k) {
+      if (lane + 32 * k < dv) {
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          const float c = v[k][e] - mean;
+          q += c * c;
+        }
+      }
+    }
+    const float inv = 1.0f / sqrtf(warp_sum(q) / (float)d + eps);
+    uint4 *orow = out + r * dv;
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k) {
+      const int j = lane + 32 * k;
+      if (j < dv) {
+        float y[N], wv[N], bv[N];
+#pragma unroll
+        for (int e = 0; e < N; e += 4) {  // weight / bias rows are f32, 16-byte aligned per vector
+          const float4 a = w ? __ldg(reinterpret_cast<const float4 *>(w + j * N + e)) : make_float4(1, 1, 1, 1);
+          const float4 c = b ? __ldg(reinterpret_cast<const float4 *>(b + j * N + e)) : make_float4(0, 0, 0, 0);
+          wv[e] = a.x, wv[e + 1] = a.y, wv[e + 2] = a.z, wv[e + 3] = a.w;
+          bv[e] = c.x, bv[e + 1] = c.y, bv[e + 2] = c.z, bv[e + 3] = c.w;
+        }
+#pragma unroll
+        for (int e = 0; e < N; ++e) y[e] = (v[k][e] - mean) * inv * wv[e] + bv[e];
+        orow[j] = Vec<T>::store(y);
+      }
+    }
+  }
+}
+
 // LayerNorm: one block per row, two-pass mean / population variance in f32.
 __global__ void layer_norm_kernel(const void *__restrict__ x, int dti, const float *__restrict__ w,
                                   const float *__restrict__ b, float eps, void *__restrict__ out, int dto,
@@ -171,17 +297,21 @@ struct PermParams {
   long long in_stride[6];  // element stride in x of output axis k (= x's stride of axis perm[k])
   long long total;
 };
-template <typename T>
+// Index type I: 32-bit when every offset fits (cheaper divisions), else 64-bit.
+template <typename T, typename I>
 __global__ void permute_kernel(const T *__restrict__ x, T *__restrict__ out, const PermParams p) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.total;
-       i += (long long)gridDim.x * blockDim.x) {
-    long long rem = i, off = 0;
+  I shape[6], stride[6];
+#pragma unroll
+  for (int k = 0; k < 6; ++k) shape[k] = (I)p.out_shape[k], stride[k] = (I)p.in_stride[k];
+  const I total = (I)p.total;
+  for (I i = blockIdx.x * (I)blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+    I rem = i, off = 0;
 #pragma unroll
     for (int k = 5; k >= 0; --k) {
       if (k < p.rank) {
-        const long long c = rem % p.out_shape[k];
-        rem /= p.out_shape[k];
-        off += c * p.in_stride[k];
+        const I q = rem / shape[k];
+        off += (rem - q * shape[k]) * stride[k];
+        rem = q;
       }
     }
     out[i] = x[off];
@@ -241,7 +371,23 @@ int mpc_add(mpc_device *dev, const void *x, const void *y, void *out, int32_t dt
     return fail(MPC_ERR_INVALID, "mpc_add: %lld elements do not repeat a block of %lld", (long long)n_x, (long long)n_y);
   if (n_x == 0) return MPC_OK;
   if (!x || !y || !out) return fail(MPC_ERR_INVALID, "mpc_add: null pointer");
-  add_kernel<<<grid_for(dev, n_x, 256), 256, 0, stream_of(dev, s)>>>(x, y, out, dt, n_x, n_y);
+  const int vw = dt == MPC_F32 ? 4 : 8;
+  const bool aligned = !(((uintptr_t)x | (uintptr_t)y | (uintptr_t)out) & 15) && n_x % vw == 0 && n_y % vw == 0;
+  cudaStream_t st = stream_of(dev, s);
+  if (aligned) {
+    const int64_t nv = n_x / vw, nyv = n_y / vw;
+    const unsigned g = grid_for(dev, nv, 256);
+    const uint4 *xv = static_cast<const uint4 *>(x), *yv = static_cast<const uint4 *>(y);
+    uint4 *ov = static_cast<uint4 *>(out);
+    if (dt == MPC_F32)
+      add_vec_kernel<float><<<g, 256, 0, st>>>(xv, yv, ov, nv, nyv);
+    else if (dt == MPC_BF16)
+      add_vec_kernel<__nv_bfloat16><<<g, 256, 0, st>>>(xv, yv, ov, nv, nyv);
+    else
+      add_vec_kernel<__half><<<g, 256, 0, st>>>(xv, yv, ov, nv, nyv);
+  } else {
+    add_kernel<<<grid_for(dev, n_x, 256), 256, 0, st>>>(x, y, out, dt, n_x, n_y);
+  }
   dev->launches++;
   return check_launch(dev, "add_kernel");
 }
@@ -254,9 +400,40 @@ int mpc_layer_norm(mpc_device *dev, const void *x, int32_t dti, const float *wei
   if (rows < 0 || d < 0) return fail(MPC_ERR_INVALID, "mpc_layer_norm: negative extent");
   if (rows == 0 || d == 0) return MPC_OK;
   if (!x || !out) return fail(MPC_ERR_INVALID, "mpc_layer_norm: null pointer");
+  cudaStream_t st = stream_of(dev, s);
+  const int vw = dti == MPC_F32 ? 4 : 8;
+  const int64_t per_lane = (d / vw + 31) / 32;  // 16-byte vectors each lane holds in registers
+  if (dti == dto && d % vw == 0 && per_lane <= 8 && !(((uintptr_t)x | (uintptr_t)out) & 15) &&
+      !(((uintptr_t)weight | (uintptr_t)bias) & 15)) {
+    const int64_t blocks_needed = (rows + 7) / 8;  // 8 warps (rows) per 256-thread block
+    const int64_t cap = (int64_t)dev->prop.multiProcessorCount * 16;
+    const unsigned g = (unsigned)(blocks_needed < cap ? blocks_needed : cap);
+    const uint4 *xv = static_cast<const uint4 *>(x);
+    uint4 *ov = static_cast<uint4 *>(out);
+    const int dd = (int)d;
+    // the register footprint follows the row length (fewer registers, more rows in flight)
+#define MPC_LN(T)                                                                                      \
+  switch (per_lane) {                                                                                  \
+    case 1: layer_norm_warp_kernel<T, 1><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
+    case 2: layer_norm_warp_kernel<T, 2><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
+    case 3: layer_norm_warp_kernel<T, 3><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
+    case 4: layer_norm_warp_kernel<T, 4><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
+    default: layer_norm_warp_kernel<T, 8><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
+  }
+    if (dti == MPC_F32) {
+      MPC_LN(float)
+    } else if (dti == MPC_BF16) {
+      MPC_LN(__nv_bfloat16)
+    } else {
+      MPC_LN(__half)
+    }
+#undef MPC_LN
+    dev->launches++;
+    return check_launch(dev, "layer_norm_warp_kernel");
+  }
   const unsigned grid = (unsigned)(rows < (int64_t)dev->prop.multiProcessorCount * 16 ? rows
                                                                                       : dev->prop.multiProcessorCount * 16);
-  layer_norm_kernel<<<grid, 256, 0, stream_of(dev, s)>>>(x, dti, weight, bias, eps, out, dto, rows, d);
+  layer_norm_kernel<<<grid, 256, 0, st>>>(x, dti, weight, bias, eps, out, dto, rows, d);
   dev->launches++;
   return check_launch(dev, "layer_norm_kernel");
 }
@@ -342,12 +519,21 @@ int mpc_transpose(mpc_device *dev, const void *x, void *out, int32_t elem_bytes,
   }
   cudaStream_t st = stream_of(dev, s);
   const unsigned grid = grid_for(dev, p.total, 256);
+  // 32-bit indexing when the element count (and so every offset) stays below 2^31 with the grid
+  // stride added.
+  const bool small = p.total + (long long)grid * 256 < (1ll << 31);
   switch (eb) {
-    case 1: permute_kernel<uint8_t><<<grid, 256, 0, st>>>((const uint8_t *)x, (uint8_t *)out, p); break;
-    case 2: permute_kernel<uint16_t><<<grid, 256, 0, st>>>((const uint16_t *)x, (uint16_t *)out, p); break;
-    case 4: permute_kernel<uint32_t><<<grid, 256, 0, st>>>((const uint32_t *)x, (uint32_t *)out, p); break;
-    case 8: permute_kernel<uint2><<<grid, 256, 0, st>>>((const uint2 *)x, (uint2 *)out, p); break;
-    default: permute_kernel<uint4><<<grid, 256, 0, st>>>((const uint4 *)x, (uint4 *)out, p); break;
+#define MPC_PERMUTE(T)                                                                  \
+  if (small)                                                                            \
+    permute_kernel<T, uint32_t><<<grid, 256, 0, st>>>((const T *)x, (T *)out, p);       \
+  else                                                                                  \
+    permute_kernel<T, long long><<<grid, 256, 0, st>>>((const T *)x, (T *)out, p);
+    case 1: MPC_PERMUTE(uint8_t) break;
+    case 2: MPC_PERMUTE(uint16_t) break;
+    case 4: MPC_PERMUTE(uint32_t) break;
+    case 8: MPC_PERMUTE(uint2) break;
+    default: MPC_PERMUTE(uint4) break;
+#undef MPC_PERMUTE
   }
   dev->launches++;
   return check_launch(dev, "permute_kernel");

@@ -23,7 +23,7 @@ STATUS_NAMES = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "OOM", 4: "CUDA", 5:
 F32, F16, BF16, I32, BOOL = range(5)
 DTYPE_CODES = {"f32": F32, "f16": F16, "bf16": BF16, "i32": I32, "bool": BOOL}
 DTYPE_BYTES = {F32: 4, F16: 2, BF16: 2, I32: 4, BOOL: 1}
-EPI_BIAS, EPI_GELU = 1, 2
+EPI_BIAS, EPI_GELU, EPI_RESIDUAL = 1, 2, 4
 B_KN, B_NK = 0, 1
 MASK_NONE, MASK_BOOL, MASK_ADD = 0, 1, 2
 
@@ -90,6 +90,7 @@ SIGNATURES = {
     "mpc_sync": [_dev],
     "mpc_launch_count": [_dev, C.POINTER(_u64)],
     "mpc_gemm": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
+    "mpc_gemm_residual": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp, _vp],
     "mpc_gemm_f32_noalloc": [C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
     "mpc_sdpa": [_dev, C.POINTER(SdpaDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "mpc_softmax": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, _vp],

@@ -6,9 +6,9 @@ for the GEMM / attention path: transfers (``fromHost`` / ``read``, async), lifet
 ``matmul``, ``linear``, ``sdpa``, ``layerNorm``, ``embedding``.
 
 Lazy inside, eager-observable (RFC 0001 §12 Q1, as the MLX and WebGPU backends): ``matmul`` and
-``linear`` return a handle whose GEMM has not run yet; an ``add`` of a bias row and a ``gelu``
-applied to that handle fold into the GEMM's epilogue, so ``x.matmul(w).add(b).gelu()`` is one
-kernel. Anything that reads the handle (another op, ``read``, ``flush``) runs it. Shape and dtype
+``linear`` return a handle whose GEMM has not run yet; an ``add`` of a bias row, a ``gelu`` and
+then an ``add`` of a same-shape array (a residual) applied to that handle fold into the GEMM's
+epilogue, so ``x.matmul(w).add(b).gelu()`` and ``h.add(x.matmul(w))`` are one kernel each. Anything that reads the handle (another op, ``read``, ``flush``) runs it. Shape and dtype
 errors are raised at the call site.
 """
 from __future__ import annotations
@@ -49,6 +49,42 @@ def host(dtype: str, shape, data) -> HostTensor:
     return HostTensor(dtype, shape, np.ascontiguousarray(arr).reshape(-1))
 
 
+class _Slice:
+    """A byte range of a DeviceBuffer, used as a buffer: views at an offset (``split``) share and
+    keep alive the block they point into."""
+
+    __slots__ = ("base", "offset")
+
+    def __init__(self, base, offset: int):
+        self.base, self.offset = base, int(offset)
+
+    @property
+    def ptr(self) -> int:
+        return self.base.ptr + self.offset
+
+    def retain(self) -> "_Slice":
+        self.base.retain()
+        return self
+
+    def release(self) -> None:
+        self.base.release()
+
+
+class _Borrowed:
+    """Device memory owned elsewhere, used as a buffer (retain / release do nothing)."""
+
+    __slots__ = ("ptr",)
+
+    def __init__(self, ptr: int):
+        self.ptr = int(ptr)
+
+    def retain(self) -> "_Borrowed":
+        return self
+
+    def release(self) -> None:
+        pass
+
+
 @dataclass
 class _PendingGemm:
     """A GEMM not yet run. It holds references to its operands' buffers, so disposing the operand
@@ -66,15 +102,16 @@ class _PendingGemm:
     bias: DeviceBuffer | None = None
     bias_dtype: str = "f32"
     epilogue: int = 0
+    resid: DeviceBuffer | None = None  # added last (MPC_EPI_RESIDUAL), in the output dtype
 
     def retain(self) -> "_PendingGemm":
-        for b in (self.a, self.b, self.bias):
+        for b in (self.a, self.b, self.bias, self.resid):
             if b is not None:
                 b.retain()
         return self
 
     def release(self) -> None:
-        for b in (self.a, self.b, self.bias):
+        for b in (self.a, self.b, self.bias, self.resid):
             if b is not None:
                 b.release()
 
@@ -192,6 +229,13 @@ class CudaBackend:
     def dispose(self, t: CudaTensor) -> None:
         t._release()
 
+    def external(self, ptr: int, shape, dtype: str) -> CudaTensor:
+        """A handle over device memory this backend does not own (another allocator's tensor);
+        the caller keeps that memory alive while the handle is in use."""
+        if dtype not in STORAGE:
+            raise TypeError(f"tensor-cuda: external: unsupported dtype {dtype}")
+        return self._make(shape, dtype, _Borrowed(ptr))
+
     def scope(self, fn):
         created: set = set()
         self._scopes.append(created)
@@ -259,6 +303,23 @@ class CudaBackend:
         _ = x.ptr
         return self._make(shape, x.dtype, x._buf.retain())  # a view sharing the buffer
 
+    def split(self, x: CudaTensor, sections: int, axis: int = 0) -> list:
+        """Equal parts along ``axis`` (Backend.split). Along the leading axis (or one behind
+        leading 1s) the parts are views sharing x's memory; other axes are not supported here."""
+        self._check_live(x)
+        nd = len(x.shape)
+        ax = axis % nd
+        if any(d != 1 for d in x.shape[:ax]):
+            raise NotImplementedError("tensor-cuda: split: only along the leading non-unit axis")
+        if sections <= 0 or x.shape[ax] % sections:
+            raise ValueError(f"tensor-cuda: split: {x.shape[ax]} is not divisible into {sections} parts")
+        _ = x.ptr
+        part = x.shape[ax] // sections
+        shape = x.shape[:ax] + (part,) + x.shape[ax + 1:]
+        step = x.nbytes // sections
+        base, off = (x._buf.base, x._buf.offset) if isinstance(x._buf, _Slice) else (x._buf, 0)
+        return [self._make(shape, x.dtype, _Slice(base, off + i * step).retain()) for i in range(sections)]
+
     def transpose(self, x: CudaTensor, perm=None) -> CudaTensor:
         """Axis permutation (default: reversed), like numpy.transpose (device-array.ts:457-471)."""
         self._check_live(x)
@@ -296,12 +357,21 @@ class CudaBackend:
         if x.size < y.size:  # add is commutative: keep the larger operand first
             x, y = y, x
         pg = x._pending
-        bias_like = pg is not None and not (pg.epilogue & (F.EPI_BIAS | F.EPI_GELU)) and y.size == pg.n and \
+        done = F.EPI_BIAS | F.EPI_GELU | F.EPI_RESIDUAL
+        bias_like = pg is not None and not (pg.epilogue & done) and y.size == pg.n and \
             all(s == 1 for s in y.shape[:-1]) and y.shape[-1] == pg.n and len(y.shape) <= len(x.shape)
         if bias_like:  # fold the bias row into the pending GEMM's epilogue
             _ = y.ptr
             folded = replace(pg, bias=y._buf, bias_dtype=y.dtype, epilogue=pg.epilogue | F.EPI_BIAS).retain()
             return self._make(x.shape, x.dtype, pending=folded)
+        if x is not y and x.shape == y.shape:
+            # a residual add: fold the other operand into a pending GEMM's epilogue (added last)
+            for a, r in ((x, y), (y, x)):
+                pa = a._pending
+                if pa is not None and not (pa.epilogue & F.EPI_RESIDUAL):
+                    _ = r.ptr
+                    folded = replace(pa, resid=r._buf, epilogue=pa.epilogue | F.EPI_RESIDUAL).retain()
+                    return self._make(a.shape, a.dtype, pending=folded)
         n_x, n_y = P.add_plan(x.shape, y.shape)
         out = self._alloc(x.shape, x.dtype)
         F.call("mpc_add", self.device.handle, C.c_void_p(x.ptr), C.c_void_p(y.ptr), C.c_void_p(out._buf.ptr),
@@ -313,7 +383,7 @@ class CudaBackend:
         if x.dtype not in FLOAT:
             raise TypeError(f"tensor-cuda: gelu: float dtypes only, got {x.dtype}")
         pg = x._pending
-        if pg is not None and not (pg.epilogue & F.EPI_GELU):  # fold into the pending GEMM
+        if pg is not None and not (pg.epilogue & (F.EPI_GELU | F.EPI_RESIDUAL)):  # fold into the pending GEMM
             return self._make(x.shape, x.dtype, pending=replace(pg, epilogue=pg.epilogue | F.EPI_GELU).retain())
         out = self._alloc(x.shape, x.dtype)
         F.call("mpc_gelu", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(out._buf.ptr),
@@ -390,7 +460,12 @@ class CudaBackend:
         out = self.device.alloc(t.nbytes)
         desc = gemm_desc(pg.m, pg.n, pg.k, F.DTYPE_CODES[pg.dtype_in], F.DTYPE_CODES[t.dtype], pg.b_layout,
                          pg.epilogue, 1.0, pg.batch_shape, pg.a_strides, pg.b_strides)
-        self.device.gemm(desc, pg.a.ptr, pg.b.ptr, out.ptr, bias_ptr)
+        if pg.resid is not None:
+            F.call("mpc_gemm_residual", self.device.handle, C.byref(desc), C.c_void_p(pg.a.ptr),
+                   C.c_void_p(pg.b.ptr), C.c_void_p(out.ptr), C.c_void_p(bias_ptr) if bias_ptr else None,
+                   C.c_void_p(pg.resid.ptr), None)
+        else:
+            self.device.gemm(desc, pg.a.ptr, pg.b.ptr, out.ptr, bias_ptr)
         if tmp is not None:
             tmp.release()
         pg.release()

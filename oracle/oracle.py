@@ -290,6 +290,46 @@ def embedding(table, ids) -> np.ndarray:
     return out
 
 
+def round_bf16(x) -> np.ndarray:
+    """What a bf16 store keeps of an f32 value (round to nearest even), back in f32."""
+    b = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    bits = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint32) << 16
+    return bits.astype(np.uint32).view(np.float32).reshape(np.shape(x))
+
+
+def gpt2_forward(w: dict, ids, n_layer: int, n_head: int, eps: float = 1e-5, store=round_bf16,
+                 threads: int = 1) -> np.ndarray:
+    """A GPT-2-shaped forward composed from the reference's CPU ops: token + position
+    ``takeRows``, then per layer the pre-norm block of ``TransformerEncoderLayer.forward``
+    (packages/tensor-autograd/src/transformer.ts:320-333, normFirst) with ``MultiheadAttention``'s
+    packed in-projection and head split / merge (transformer.ts:223-241) under a causal mask,
+    exact GELU, and a final LayerNorm and tied LM head (``linearNT`` with the token table).
+    ``w`` holds f32 arrays under GPT-2's parameter names; ``store`` is applied to every op's
+    output (the device stores bf16). Returns logits [B, L, vocab]."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    B, L = ids.shape
+    D = w["wte"].shape[1]
+    Dh = D // n_head
+    causal = np.tril(np.ones((L, L), np.bool_)).reshape(1, 1, L, L)
+    x = store(add_f32(embedding(w["wte"], ids), embedding(w["wpe"], np.arange(L, dtype=np.int32))))
+    x = x.reshape(B * L, D)
+    for i in range(n_layer):
+        p = f"h.{i}."
+        h = store(layer_norm(x, w[p + "ln_1.weight"], w[p + "ln_1.bias"], eps))
+        qkv = store(linear(h, w[p + "attn.in_proj_weight"], w[p + "attn.in_proj_bias"], threads=threads))
+        q, k, v = (np.ascontiguousarray(t) for t in np.transpose(qkv.reshape(B, L, 3, n_head, Dh), (2, 0, 3, 1, 4)))
+        a = store(sdpa(q, k, v, causal, 1.0 / np.sqrt(Dh), threads=threads))
+        merged = np.ascontiguousarray(np.transpose(a, (0, 2, 1, 3))).reshape(B * L, D)
+        o = store(linear(merged, w[p + "attn.out_proj.weight"], w[p + "attn.out_proj.bias"], threads=threads))
+        x1 = store(add_f32(x, o))
+        h2 = store(layer_norm(x1, w[p + "ln_2.weight"], w[p + "ln_2.bias"], eps))
+        f = store(gelu(linear(h2, w[p + "mlp.fc.weight"], w[p + "mlp.fc.bias"], threads=threads)))
+        g = store(linear(f, w[p + "mlp.proj.weight"], w[p + "mlp.proj.bias"], threads=threads))
+        x = store(add_f32(x1, g))
+    h = store(layer_norm(x, w["ln_f.weight"], w["ln_f.bias"], eps))
+    return store(linear(h, w["wte"], threads=threads)).reshape(B, L, -1)
+
+
 def gemm_nt_f64(a: np.ndarray, b_nt: np.ndarray, threads: int = 1) -> np.ndarray:
     """Raw ``gemmNT`` over packed f64 panels (kernels.ts:299-362): a [M,K], b_nt [N,K]."""
     a = np.ascontiguousarray(a, np.float64)

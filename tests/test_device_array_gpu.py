@@ -190,3 +190,20 @@ def test_transpose_like_numpy(dev):
     assert np.array_equal(got, np.transpose(big, [2, 0, 3, 1, 4]))
     with pytest.raises(ValueError, match="permutation"):
         dev.from_numpy(x).transpose([0, 0, 1])
+
+
+def test_residual_add_folds_into_the_gemm(dev):
+    """h.add(x.matmul(w)) and x.matmul(w).add(h): one GEMM launch with the residual in its
+    epilogue; values as the oracle's matmul + add."""
+    m, k, n = 96, 64, 80
+    g = lambda shape, s: O.normal_f32(int(np.prod(shape)), s, 0, 0.3).reshape(shape)
+    x, ex = up(dev, g((m, k), 1), "bf16")
+    w, ew = up(dev, g((k, n), 2), "bf16")
+    h, eh = up(dev, g((m, n), 3), "bf16")
+    want = O.add_f32(O.matmul(ex, ew), eh).astype(np.float64)
+    for expr in (lambda: h.add(x.matmul(w)), lambda: x.matmul(w).add(h)):
+        before = dev.device.launch_count()
+        y = expr()
+        y.eval()
+        assert dev.device.launch_count() - before == 1
+        close(run(y.toTensor()).astype(np.float64), want, "bf16")

@@ -144,3 +144,33 @@ def test_gemm_k_zero_and_empty(dev):
     got = run_gemm(dev, np.zeros((3, 0), np.float32), np.zeros((0, 5), np.float32), "f32", "f32", F.B_KN, 3, 5, 0,
                    bias, F.EPI_BIAS)
     assert np.array_equal(got.reshape(3, 5), np.tile(bias, (3, 1)))
+
+
+@pytest.mark.parametrize("dtype_in,dtype_out,n,in_place", [("bf16", "bf16", 264, False), ("bf16", "bf16", 100, False),
+                                                            ("f16", "f32", 264, True), ("bf16", "bf16", 264, True),
+                                                            ("f32", "f32", 72, False)])
+def test_gemm_residual_epilogue(dev, dtype_in, dtype_out, n, in_place):
+    """C = A·Wᵀ + bias + R (the transformer residual) in the epilogue: against the oracle's
+    linear + add with the device rounding once; R may be C itself; unaligned rows (n=100 bf16)
+    take the scalar path."""
+    import ctypes as C
+    from tensor_cuda import _ffi as F
+    from tensor_cuda.runtime import gemm_desc
+    m, k = 200, 96
+    a_up, a_ex = to_device_dtype(O.lcg_gemm(m * k, 31).reshape(m, k), dtype_in)
+    w_up, w_ex = to_device_dtype(O.lcg_gemm(n * k, 32).reshape(n, k), dtype_in)
+    bias = O.normal_f32(n, 33, 0, 0.5)
+    r_up, r_ex = to_device_dtype(O.lcg_gemm(m * n, 34).reshape(m, n), dtype_out)
+    da, dw, dbias, dr = dev.upload(a_up), dev.upload(w_up), dev.upload(bias), dev.upload(r_up)
+    dc = dr if in_place else dev.alloc(m * n * F.DTYPE_BYTES[F.DTYPE_CODES[dtype_out]])
+    desc = gemm_desc(m, n, k, F.DTYPE_CODES[dtype_in], F.DTYPE_CODES[dtype_out], F.B_NK, F.EPI_BIAS | F.EPI_RESIDUAL)
+    F.call("mpc_gemm_residual", dev.handle, C.byref(desc), C.c_void_p(da.ptr), C.c_void_p(dw.ptr),
+           C.c_void_p(dc.ptr), C.c_void_p(dbias.ptr), C.c_void_p(dr.ptr), None)
+    dev.sync()
+    got = from_device_dtype(dev.download(dc.ptr, m * n * F.DTYPE_BYTES[F.DTYPE_CODES[dtype_out]],
+                                         NP_STORAGE[dtype_out], (m, n)), dtype_out).astype(np.float64)
+    want = O.linear(a_ex, w_ex, bias).astype(np.float64) + r_ex.astype(np.float64)
+    absprod = O.matmul(np.abs(a_ex), np.ascontiguousarray(np.abs(w_ex).T)).astype(np.float64)
+    assert np.all(np.abs(got - want) <= gemm_bound(want, absprod + np.abs(r_ex), dtype_in, dtype_out))
+    with pytest.raises(F.MpcError, match="mpc_gemm_residual"):
+        dev.gemm(desc, da.ptr, dw.ptr, dc.ptr, dbias.ptr)
