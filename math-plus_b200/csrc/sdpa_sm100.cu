@@ -3,7 +3,10 @@
 // path builds the full Lq x Lk f64 score panel per head (packages/tensor-core/src/nn-kernels.ts:179-239).
 //
 // Tensor-core path (f16 / bf16, head dim 64 or 128, 16-byte aligned operands):
-//   one CTA per (batch, head, 256 query rows) = two 128-row Q tiles sharing every K/V tile; 12 warps:
+//   persistent CTAs (at most one per SM) walk units of (batch, head, 256 query rows) = two 128-row
+//   Q tiles sharing every K/V tile, in pairs of a heavy and a light causal q-block so that every
+//   pair is the same work. Across units the producer loads the next Q as soon as the last QK has
+//   read the current one, and the next unit's QK products overlap the current output; 12 warps:
 //   warps 0-3 / 4-7  online softmax of Q tile 0 / 1, one thread per query row: tcgen05.ld the S row,
 //                    scale (folded with log2 e), mask, row max, exp2, row sum; P (same type as V) is
 //                    tcgen05.st'd back over the first half of the S columns; the O accumulator is
@@ -30,6 +33,7 @@ struct Params {
   int B, H, Hk, Lq, Lk, D;
   int rep;       // H / Hk
   int q_blocks;  // ceil(Lq / 256)
+  int n_units;  // B * H * q_blocks
   int causal;
   float scale_log2;  // scale * log2(e)
   int mask_kind;
@@ -71,6 +75,35 @@ __device__ __forceinline__ float mask_add(const Params &p, int b, int h, int q, 
   return static_cast<const float *>(p.mask)[off] * 1.4426950408889634f;
 }
 
+// One unit of work: 256 query rows (two 128-row Q tiles) of one (batch, head).
+struct Unit {
+  int bh, b, h, kvh, q0;
+  bool valid1;
+  int last0, last1, n_kv;
+};
+
+// Units are numbered head-major; within a head the q-blocks alternate heavy and light
+// (QB-1, 0, QB-2, 1, ...), and each CTA takes units in pairs (2i, 2i+1), so under a causal mask
+// every pair carries the same work. Returns false past the last unit.
+__device__ __forceinline__ bool unit_of(const Params &p, int k, Unit &w) {
+  // 32-bit arithmetic: the host keeps 2 * n_units + 2 * gridDim.x below 2^31.
+  const unsigned u = 2u * (blockIdx.x + (unsigned)(k >> 1) * gridDim.x) + (unsigned)(k & 1);
+  if (u >= (unsigned)p.n_units) return false;
+  const unsigned qbn = (unsigned)p.q_blocks;
+  w.bh = (int)(u / qbn);
+  const int r = (int)(u - (unsigned)w.bh * qbn);
+  const int qb = (r & 1) ? (r >> 1) : qbn - 1 - (r >> 1);
+  w.b = w.bh / p.H;
+  w.h = w.bh - w.b * p.H;
+  w.kvh = w.b * p.Hk + w.h / p.rep;
+  w.q0 = qb * 256;
+  w.valid1 = w.q0 + 128 < p.Lq;
+  w.last0 = last_kv(p, w.q0);
+  w.last1 = w.valid1 ? last_kv(p, w.q0 + 128) : -1;
+  w.n_kv = max(w.last0, w.last1) + 1;
+  return true;
+}
+
 template <int D>
 __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Maps maps, const Params p) {
   using C = Cfg<D>;
@@ -80,30 +113,22 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
   uint8_t *skv = smem + 2 * C::TILE;  // ring of SLOTS K/V tiles
   uint64_t *bars = reinterpret_cast<uint64_t *>(skv + C::SLOTS * C::TILE);
   uint64_t *q_full = bars;
-  uint64_t *kv_full = bars + 1;
+  uint64_t *q_empty = bars + 1;
+  uint64_t *kv_full = bars + 2;
   uint64_t *kv_empty = kv_full + C::SLOTS;
   uint64_t *s_ready = kv_empty + C::SLOTS;  // [2]
   uint64_t *p_ready = s_ready + 2;          // [2]
   uint64_t *o_ready = p_ready + 2;          // [2]
-  uint64_t *drain = o_ready + 2;
+  uint64_t *o_free = o_ready + 2;           // [2]
+  uint64_t *drain = o_free + 2;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Head-major order: the CTAs running together share a few heads' K/V in L2; within a head the
-  // heaviest (causal) query blocks go first, so the grid ends on light blocks.
-  const int bh = (int)(blockIdx.x / p.q_blocks);
-  const int qb = p.q_blocks - 1 - (int)(blockIdx.x % p.q_blocks);
-  const int b = bh / p.H, h = bh % p.H;
-  const int kvh = b * p.Hk + h / p.rep;
-  const int q0 = qb * 256;
-  const bool valid1 = q0 + 128 < p.Lq;
-  const int last0 = last_kv(p, q0);
-  const int last1 = valid1 ? last_kv(p, q0 + 128) : -1;
-  const int n_kv = max(last0, last1) + 1;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int s = 0; s < C::SLOTS; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
@@ -112,6 +137,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
       mbar_init(&s_ready[t], 1);
       mbar_init(&p_ready[t], 4);
       mbar_init(&o_ready[t], 1);
+      mbar_init(&o_free[t], 4);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -129,49 +155,51 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
   // Register reconfiguration (at the head of each role's branch): the load / MMA warpgroup
   // gives registers to the two softmax warpgroups, which keep a whole 128-key score row in
   // registers. Launched at 168 per thread (the host checks):
-  // 2 x 128 x 224 + 128 x 56 = 64512 = 384 x 168.
+  // 2 x 128 x 208 + 128 x 88 = 64512 = 384 x 168.
   if (warp >= 10) {
-    reg_dealloc<56>();  // the warpgroup's two spare warps only wait for the end
+    reg_dealloc<88>();  // the warpgroup's two spare warps only wait for the end
   } else if (warp == 8) {
-    reg_dealloc<56>();
+    reg_dealloc<88>();
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_desc(&maps.q);
       tma_prefetch_desc(&maps.k);
       tma_prefetch_desc(&maps.v);
-      const int nq = valid1 ? 2 : 1;
-      mbar_expect_tx(q_full, nq * C::TILE);
-      for (int t = 0; t < nq; ++t)
-        for (int s = 0; s < C::NSUB; ++s)
-          tma_load_3d(&maps.q, q_full, sq + t * C::TILE + s * C::SUB, s * 64, q0 + 128 * t, bh);
-      int issued = 0;
+      int ring = 0, q_loads = 0;
       bool ok = true;
-      for (int i = 0; ok && i < 2 * n_kv; ++i) {
-        const int slot = i % C::SLOTS;
-        const uint32_t ph = (i / C::SLOTS) & 1;
-        if (!mbar_wait(&kv_empty[slot], ph ^ 1, abort_flag, p.err, kErrWaitProducer, p.timeout_ns)) {
-          ok = false;
+      Unit w;
+      for (int k = 0; ok && unit_of(p, k, w); ++k) {
+        // Q of the previous unit is free once its last QK products have run.
+        if (k > 0 && !(ok = mbar_wait(q_empty, (k - 1) & 1, abort_flag, p.err, kErrWaitProducer, p.timeout_ns)))
           break;
+        const int nq = w.valid1 ? 2 : 1;
+        mbar_expect_tx(q_full, nq * C::TILE);
+        for (int t = 0; t < nq; ++t)
+          for (int s = 0; s < C::NSUB; ++s)
+            tma_load_3d(&maps.q, q_full, sq + t * C::TILE + s * C::SUB, s * 64, w.q0 + 128 * t, w.bh);
+        ++q_loads;
+        for (int i = 0; i < 2 * w.n_kv; ++i, ++ring) {
+          const int slot = ring % C::SLOTS;
+          if (!(ok = mbar_wait(&kv_empty[slot], ((ring / C::SLOTS) & 1) ^ 1, abort_flag, p.err, kErrWaitProducer,
+                               p.timeout_ns)))
+            break;
+          const CUtensorMap *map = (i & 1) ? &maps.v : &maps.k;
+          mbar_expect_tx(&kv_full[slot], C::TILE);
+          for (int s = 0; s < C::NSUB; ++s)
+            tma_load_3d(map, &kv_full[slot], skv + slot * C::TILE + s * C::SUB, s * 64, (i >> 1) * 128, w.kvh);
         }
-        const CUtensorMap *map = (i & 1) ? &maps.v : &maps.k;
-        mbar_expect_tx(&kv_full[slot], C::TILE);
-        for (int s = 0; s < C::NSUB; ++s)
-          tma_load_3d(map, &kv_full[slot], skv + slot * C::TILE + s * C::SUB, s * 64, (i >> 1) * 128, kvh);
-        ++issued;
       }
       if (!ok) {  // let the copies in flight land before shared memory is released
         volatile int never = 0;
-        mbar_wait(q_full, 0, &never, p.err, kErrWaitProducer, p.timeout_ns);
-        const int n = issued < C::SLOTS ? issued : C::SLOTS;
-        for (int i = issued - n; i < issued; ++i)
+        if (q_loads > 0) mbar_wait(q_full, (q_loads - 1) & 1, &never, p.err, kErrWaitProducer, p.timeout_ns);
+        for (int i = ring > C::SLOTS ? ring - C::SLOTS : 0; i < ring; ++i)
           mbar_wait(&kv_full[i % C::SLOTS], (i / C::SLOTS) & 1, &never, p.err, kErrWaitProducer, p.timeout_ns);
       }
     }
   } else if (warp == 9) {
     // ---------------- MMA issuer ----------------
-    reg_dealloc<56>();
-    if (lane == 0 && n_kv > 0) {
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns);
+    reg_dealloc<88>();
+    if (lane == 0) {
       const uint32_t q_addr = smem_u32(sq);
       auto qk = [&](int t, int slot) {
         const uint32_t a0 = q_addr + t * C::TILE, b0 = smem_u32(skv + slot * C::TILE);
@@ -189,50 +217,59 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
           mma_f16_ts(tmem + 256 + t * D, tmem + t * 128 + kk * 8, make_sdesc(v0 + kk * 2048, C::SUB, 1024),
                      p.idesc_pv, (first && kk == 0) ? 0u : 1u);
       };
-      auto need = [&](int t, int j) { return j <= (t ? last1 : last0); };
-      // K_j is ring item 2j, V_j item 2j+1.
+      int ring = 0;                 // K/V ring items consumed so far (K_j, V_j of every unit in order)
+      int pv_cnt0 = 0, pv_cnt1 = 0;  // PV products issued per Q tile (p_ready phases)
+      bool ok = true;
       auto wait_item = [&](int i) {
         return mbar_wait(&kv_full[i % C::SLOTS], (i / C::SLOTS) & 1, abort_flag, p.err, kErrWaitConsumer,
                          p.timeout_ns);
       };
-      if (ok) ok = wait_item(0);
-      if (ok) {
+      Unit w;
+      for (int k = 0; ok && unit_of(p, k, w); ++k) {
+        auto need = [&](int t, int j) { return j <= (t ? w.last1 : w.last0); };
+        const int base = ring;  // K_j is ring item base + 2j, V_j item base + 2j + 1
+        auto do_pv = [&](int t, int j, int sv, int &cnt) -> bool {
+          if (j == 0 && k > 0) {  // O_t still holds the previous unit until its output has been read
+            if (!mbar_wait(&o_free[t], (k - 1) & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns)) return false;
+          }
+          if (!mbar_wait(&p_ready[t], cnt & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns)) return false;
+          tc_fence_after();
+          pv(t, sv, j == 0);
+          tc_commit(&o_ready[t]);
+          ++cnt;
+          return true;
+        };
+        if (!(ok = mbar_wait(q_full, k & 1, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns))) break;
+        if (!(ok = wait_item(base))) break;
         tc_fence_after();
         if (need(0, 0)) {
-          qk(0, 0);
+          qk(0, base % C::SLOTS);
           tc_commit(&s_ready[0]);
         }
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int sk = (2 * j) % C::SLOTS, sv = (2 * j + 1) % C::SLOTS;
-        if (need(1, j)) {
-          qk(1, sk);
-          tc_commit(&s_ready[1]);
-        }
-        tc_commit(&kv_empty[sk]);  // K_j is consumed once both QK products have run
-        if (!(ok = wait_item(2 * j + 1))) break;
-        tc_fence_after();
-        if (need(0, j)) {
-          if (!(ok = mbar_wait(&p_ready[0], j & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
-          tc_fence_after();
-          pv(0, sv, j == 0);
-          tc_commit(&o_ready[0]);
-        }
-        if (j + 1 < n_kv) {
-          if (!(ok = wait_item(2 * (j + 1)))) break;
-          tc_fence_after();
-          if (need(0, j + 1)) {
-            qk(0, (2 * (j + 1)) % C::SLOTS);
-            tc_commit(&s_ready[0]);
+        for (int j = 0; j < w.n_kv; ++j) {
+          const int sk = (base + 2 * j) % C::SLOTS, sv = (base + 2 * j + 1) % C::SLOTS;
+          if (need(1, j)) {
+            qk(1, sk);
+            tc_commit(&s_ready[1]);
           }
-        }
-        if (need(1, j)) {
-          if (!(ok = mbar_wait(&p_ready[1], j & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
+          // K_j is consumed once both QK products have run; after the last QK, so is Q.
+          tc_commit(&kv_empty[sk]);
+          if (j + 1 == w.n_kv) tc_commit(q_empty);
+          if (!(ok = wait_item(base + 2 * j + 1))) break;
           tc_fence_after();
-          pv(1, sv, j == 0);
-          tc_commit(&o_ready[1]);
+          if (need(0, j) && !(ok = do_pv(0, j, sv, pv_cnt0))) break;
+          if (j + 1 < w.n_kv) {
+            if (!(ok = wait_item(base + 2 * (j + 1)))) break;
+            tc_fence_after();
+            if (need(0, j + 1)) {
+              qk(0, (base + 2 * (j + 1)) % C::SLOTS);
+              tc_commit(&s_ready[0]);
+            }
+          }
+          if (need(1, j) && !(ok = do_pv(1, j, sv, pv_cnt1))) break;
+          tc_commit(&kv_empty[sv]);
         }
-        tc_commit(&kv_empty[sv]);
+        ring = base + 2 * w.n_kv;
       }
       tc_commit(drain);
       volatile int never = 0;
@@ -240,152 +277,166 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
     }
   } else {
     // ---------------- softmax + correction + output (warps 0-7) ----------------
-    reg_alloc<224>();
+    reg_alloc<208>();
     const int t = warp >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const int q = q0 + 128 * t + row;
-    const int last = t ? last1 : last0;
-    const bool tile_valid = t == 0 || valid1;
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + t * 128;
     const uint32_t o_addr = tmem + lane_base + 256 + t * D;
-    float m = -INFINITY, l = 0.0f;
+    int s_cnt = 0;   // S tiles of this Q tile waited for so far (s_ready phases)
+    int pv_cnt = 0;  // PV products of this Q tile completed before the current unit (o_ready phases)
     bool ok = true;
-    if (tile_valid) {
-      for (int j = 0; j <= last; ++j) {
-        if (!(ok = mbar_wait_warp(&s_ready[t], j & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
-        tc_fence_after();
-        const int k0 = j * 128;
-        const bool edge = k0 + 127 >= p.Lk || (p.causal && k0 + 127 > q0 + 128 * t);
-        const bool masked = p.mask_kind != MPC_MASK_NONE && q < p.Lq;
-        // The whole 128-key row in registers: four loads in flight, one wait.
-        uint32_t r0[32], r1[32], r2[32], r3[32];
-        tmem_ld32(s_addr, r0);
-        tmem_ld32(s_addr + 32, r1);
-        tmem_ld32(s_addr + 64, r2);
-        tmem_ld32(s_addr + 96, r3);
-        tmem_ld_wait(r0);
-        tmem_ld_wait(r1);
-        tmem_ld_wait(r2);
-        tmem_ld_wait(r3);
-        float v[128];
+    Unit w;
+    for (int k = 0; ok && unit_of(p, k, w); ++k) {
+      const int q = w.q0 + 128 * t + row;
+      const int last = t ? w.last1 : w.last0;
+      const bool tile_valid = t == 0 || w.valid1;
+      const int b = w.b, h = w.h;
+      float m = -INFINITY, l = 0.0f;
+      if (tile_valid) {
+        for (int j = 0; j <= last; ++j) {
+          if (!(ok = mbar_wait_warp(&s_ready[t], s_cnt & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
+          ++s_cnt;
+          tc_fence_after();
+          const int k0 = j * 128;
+          const bool edge = k0 + 127 >= p.Lk || (p.causal && k0 + 127 > w.q0 + 128 * t);
+          const bool masked = p.mask_kind != MPC_MASK_NONE && q < p.Lq;
+          // The whole 128-key row in registers: four loads in flight, one wait.
+          uint32_t r0[32], r1[32], r2[32], r3[32];
+          tmem_ld32(s_addr, r0);
+          tmem_ld32(s_addr + 32, r1);
+          tmem_ld32(s_addr + 64, r2);
+          tmem_ld32(s_addr + 96, r3);
+          tmem_ld_wait(r0);
+          tmem_ld_wait(r1);
+          tmem_ld_wait(r2);
+          tmem_ld_wait(r3);
+          float v[128];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          v[e] = __uint_as_float(r0[e]);
-          v[32 + e] = __uint_as_float(r1[e]);
-          v[64 + e] = __uint_as_float(r2[e]);
-          v[96 + e] = __uint_as_float(r3[e]);
-        }
-        // Scores stay unscaled (scale > 0 commutes with the max) unless a mask must be added.
-        float scl = p.scale_log2;
-        if (edge) {
-#pragma unroll
-          for (int c = 0; c < 128; ++c) {
-            const int k = k0 + c;
-            if (k >= p.Lk || (p.causal && k > q)) v[c] = -INFINITY;
+          for (int e = 0; e < 32; ++e) {
+            v[e] = __uint_as_float(r0[e]);
+            v[32 + e] = __uint_as_float(r1[e]);
+            v[64 + e] = __uint_as_float(r2[e]);
+            v[96 + e] = __uint_as_float(r3[e]);
           }
-        }
-        if (masked || scl < 0.0f) {
+          // Scores stay unscaled (scale > 0 commutes with the max) unless a mask must be added.
+          float scl = p.scale_log2;
+          if (edge) {
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
-            v[c] = fmaf(v[c], scl, (masked && k0 + c < p.Lk) ? mask_add(p, b, h, q, k0 + c) : 0.0f);
-          scl = 1.0f;
-        }
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int c = 0; c < 128; ++c) mx[c & 3] = fmaxf(mx[c & 3], v[c]);
-        const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scl;
-        const float m_new = fmaxf(m, mt);
-        const bool grow = m_new > m + 8.0f;  // lazy rescale: P stays below 2^8 otherwise
-        if (__any_sync(0xffffffffu, grow)) {
-          const float factor = (m == -INFINITY) ? 0.0f : exp2f(m - m_new);
-          if (j > 0) {
-            if (!(ok = mbar_wait_warp(&o_ready[t], (j - 1) & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns)))
-              break;
-            tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < D / 32; ++c) {
-              uint32_t r[32];
-              tmem_ld32(o_addr + c * 32, r);
-              tmem_ld_wait(r);
-#pragma unroll
-              for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * factor);
-              tmem_st32(o_addr + c * 32, r);
+            for (int c = 0; c < 128; ++c) {
+              const int kc = k0 + c;
+              if (kc >= p.Lk || (p.causal && kc > q)) v[c] = -INFINITY;
             }
-            tmem_st_wait();
           }
-          l *= factor;
-          m = m_new;
-        }
-        const float neg_m = m == -INFINITY ? 0.0f : -m;
-        // P = exp2(s·scale - m), packed two keys per TMEM column (key 2e in the low half of column e),
-        // over the first 64 S columns (the row is already in registers). The exponentials run two
-        // at a time on the f16x2 path of the special-function unit; the argument's f16 rounding
-        // perturbs P by at most 2^-11·ln2·|x| relative (<= 0.6% for the P < 2^-8 that |x| > 8
-        // gives). The row sum stays f32.
-        float rs[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        uint32_t w0[32], w1[32];
+          if (masked || scl < 0.0f) {
 #pragma unroll
-        for (int e = 0; e < 64; ++e) {
-          const __half2 x2 = __floats2half2_rn(fmaf(v[2 * e], scl, neg_m), fmaf(v[2 * e + 1], scl, neg_m));
-          const uint32_t e2 = ex2_f16x2(*reinterpret_cast<const uint32_t *>(&x2));
-          const float2 pf = __half22float2(*reinterpret_cast<const __half2 *>(&e2));
-          rs[e & 3] += pf.x + pf.y;
-          uint32_t packed = e2;
-          if (p.dtype == MPC_BF16) {
-            __nv_bfloat162 v2 = __floats2bfloat162_rn(pf.x, pf.y);
-            packed = *reinterpret_cast<uint32_t *>(&v2);
+            for (int c = 0; c < 128; ++c)
+              v[c] = fmaf(v[c], scl, (masked && k0 + c < p.Lk) ? mask_add(p, b, h, q, k0 + c) : 0.0f);
+            scl = 1.0f;
           }
-          if (e < 32)
-            w0[e] = packed;
-          else
-            w1[e - 32] = packed;
+          float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+          for (int c = 0; c < 128; c += 2) mx[(c >> 1) & 3] = max3f(mx[(c >> 1) & 3], v[c], v[c + 1]);
+          const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scl;
+          const float m_new = fmaxf(m, mt);
+          const bool grow = m_new > m + 8.0f;  // lazy rescale: P stays below 2^8 otherwise
+          if (__any_sync(0xffffffffu, grow)) {
+            const float factor = (m == -INFINITY) ? 0.0f : exp2f(m - m_new);
+            if (j > 0) {
+              if (!(ok = mbar_wait_warp(&o_ready[t], (pv_cnt + j - 1) & 1, abort_flag, p.err, kErrWaitSoftmax,
+                                        p.timeout_ns)))
+                break;
+              tc_fence_after();
+#pragma unroll 1
+              for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(o_addr + c * 32, r);
+                tmem_ld_wait(r);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * factor);
+                tmem_st32(o_addr + c * 32, r);
+              }
+              tmem_st_wait();
+            }
+            l *= factor;
+            m = m_new;
+          }
+          const float neg_m = m == -INFINITY ? 0.0f : -m;
+          // P = exp2(s·scale - m), packed two keys per TMEM column (key 2e in the low half of column
+          // e), over the first 64 S columns (the row is already in registers). The exponentials run
+          // two at a time on the f16x2 path of the special-function unit; the argument's f16
+          // rounding perturbs P by at most 2^-11·ln2·|x| relative (<= 0.6% for the P < 2^-8 that
+          // |x| > 8 gives). The row sum stays f32 (mixed-precision adds of the f16 values).
+          float rs[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+          uint32_t w0[32], w1[32];
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const float2 a = fma2(v[2 * e], v[2 * e + 1], scl, scl, neg_m, neg_m);  // s*scale - m, two at once
+            const __half2 x2 = __floats2half2_rn(a.x, a.y);
+            const uint32_t e2 = ex2_f16x2(*reinterpret_cast<const uint32_t *>(&x2));
+            rs[e & 7] = add_f16x2_to_f32(rs[e & 7], e2);
+            uint32_t packed = e2;
+            if (p.dtype == MPC_BF16) {
+              const float2 pf = __half22float2(*reinterpret_cast<const __half2 *>(&e2));
+              __nv_bfloat162 v2 = __floats2bfloat162_rn(pf.x, pf.y);
+              packed = *reinterpret_cast<uint32_t *>(&v2);
+            }
+            if (e < 32)
+              w0[e] = packed;
+            else
+              w1[e - 32] = packed;
+          }
+          tmem_st32(s_addr, w0);
+          tmem_st32(s_addr + 32, w1);
+          l += ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_ready[t]);
         }
-        tmem_st32(s_addr, w0);
-        tmem_st32(s_addr + 32, w1);
-        l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_ready[t]);
-      }
-      // ---- output: O / l, rows below Lq ----
-      if (ok && last >= 0) ok = mbar_wait_warp(&o_ready[t], last & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns);
-      tc_fence_after();
-      if (ok && last >= 0) {
+        if (!ok) break;
+        // ---- output: O / l, rows below Lq ----
+        if (!(ok = mbar_wait_warp(&o_ready[t], (pv_cnt + last) & 1, abort_flag, p.err, kErrWaitSoftmax,
+                                  p.timeout_ns)))
+          break;
+        pv_cnt += last + 1;
+        tc_fence_after();
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        const size_t orow = ((size_t)bh * p.Lq + (size_t)q) * D;
+        const size_t orow = ((size_t)w.bh * p.Lq + (size_t)q) * D;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(o_addr + c * 32, r);
           tmem_ld_wait(r);
+          if (c + 1 == D / 32) {  // O_t is in registers: the next unit's first PV may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_free[t]);
+          }
           if (q < p.Lq) {
-            uint32_t w[16];
+            uint32_t ow[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const float a = __uint_as_float(r[2 * e]) * inv, bb = __uint_as_float(r[2 * e + 1]) * inv;
               if (p.dtype == MPC_BF16) {
                 __nv_bfloat162 v2 = __floats2bfloat162_rn(a, bb);
-                w[e] = *reinterpret_cast<uint32_t *>(&v2);
+                ow[e] = *reinterpret_cast<uint32_t *>(&v2);
               } else {
                 __half2 v2 = __floats2half2_rn(a, bb);
-                w[e] = *reinterpret_cast<uint32_t *>(&v2);
+                ow[e] = *reinterpret_cast<uint32_t *>(&v2);
               }
             }
             uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.out) + orow + c * 32);
 #pragma unroll
-            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+            for (int e = 0; e < 4; ++e) dst[e] = make_uint4(ow[4 * e], ow[4 * e + 1], ow[4 * e + 2], ow[4 * e + 3]);
           }
         }
         if (p.lse && q < p.Lq)
-          p.lse[(size_t)bh * p.Lq + q] = l > 0.0f ? (m * 0.6931471805599453f + logf(l)) : -INFINITY;
-      } else if (last < 0 && q < p.Lq && tile_valid) {
-        // No key is visible to this tile at all (Lk == 0): the fully-masked-row convention, zeros.
-        uint4 *dst = reinterpret_cast<uint4 *>(static_cast<uint16_t *>(p.out) + ((size_t)bh * p.Lq + q) * D);
-        for (int e = 0; e < D / 8; ++e) dst[e] = make_uint4(0, 0, 0, 0);
-        if (p.lse) p.lse[(size_t)bh * p.Lq + q] = -INFINITY;
+          p.lse[(size_t)w.bh * p.Lq + q] = l > 0.0f ? (m * 0.6931471805599453f + logf(l)) : -INFINITY;
+      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[t]);  // keep o_free's phases in step with the units
       }
     }
   }
@@ -507,7 +558,9 @@ int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t s
       return fail(MPC_ERR_UNSUPPORTED, "attn_kernel built with %d registers per thread (expected 168)", fa.numRegs);
     configured[ord] = true;
   }
-  const long long grid = (long long)p.q_blocks * p.B * p.H;
+  // Persistent: one CTA per SM (at most), each taking pairs of units until none is left.
+  const long long pairs = ((long long)p.n_units + 1) / 2;
+  const long long grid = pairs < dev->prop.multiProcessorCount ? pairs : dev->prop.multiProcessorCount;
   attn_kernel<D><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(maps, p);
   dev->launches++;
   return check_launch(dev, "attn_kernel");
@@ -550,6 +603,10 @@ int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void 
   p.B = (int)d->b, p.H = (int)d->h, p.Hk = (int)d->hk, p.Lq = (int)d->lq, p.Lk = (int)d->lk, p.D = (int)d->d;
   p.rep = p.H / p.Hk;
   p.q_blocks = (p.Lq + 255) / 256;
+  const long long units = (long long)p.q_blocks * p.B * p.H;
+  if (2 * units + 2 * dev->prop.multiProcessorCount >= (1ll << 31))
+    return fail(MPC_ERR_UNSUPPORTED, "mpc_sdpa: %lld units of 256 query rows (at most 2^30)", units);
+  p.n_units = (int)units;
   p.causal = d->causal ? 1 : 0;
   p.scale_log2 = d->scale * 1.4426950408889634f;
   p.mask_kind = d->mask_kind;

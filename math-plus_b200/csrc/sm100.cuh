@@ -261,6 +261,33 @@ __device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
   return y;
 }
 
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Two fused multiply-adds in one instruction: (a0, a1) * (b0, b1) + (c0, c1), round to nearest.
+__device__ __forceinline__ float2 fma2(float a0, float a1, float b0, float b1, float c0, float c1) {
+  unsigned long long a, b, c, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(c0), "f"(c1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
+// acc + (both halves of an f16x2), in f32: mixed-precision adds, no separate unpacking.
+__device__ __forceinline__ float add_f16x2_to_f32(float acc, uint32_t h2) {
+  asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %1;\n add.f32.f16 %0, lo, %0;\n add.f32.f16 %0, hi, %0;\n}\n"
+      : "+f"(acc)
+      : "r"(h2));
+  return acc;
+}
+
 // Warpgroup register reconfiguration (every warp of the warpgroup executes it).
 template <int N>
 __device__ __forceinline__ void reg_alloc() {

@@ -116,6 +116,8 @@ def test_differential_sdpa_cases(dev, golden_dir):
     (1, 2, 2, 300, 700, 128, False),     # Lq != Lk, K/V tail tile
     (2, 8, 2, 384, 384, 64, True),       # GQA, head dim 64
     (1, 3, 1, 130, 257, 64, False),      # one row in the second Q tile
+    (3, 25, 5, 800, 800, 64, True),      # 300 units on a persistent grid: CTAs walk several unit
+                                         # pairs; the last q-block of each head has no second tile
 ])
 def test_tensor_core_path_shapes(dev, dtype, B, H, Hk, Lq, Lk, D, causal):
     q = exact(O.normal_f32(B * H * Lq * D, 31).reshape(B, H, Lq, D), dtype)
