@@ -8,7 +8,7 @@
 // relative error of erfcx over t in [0, 12] (2e-8 in exact arithmetic, 4e-7 evaluated in f32).
 // t² is split into hi + lo (fma) so its rounding stays out of the exponent. Then
 //   Φ(x) = ½·erfc(t) for x <= 0,  1 - ½·erfc(t) for x > 0.
-// The tests hold it to the reference's f64 GELU (oracle) on a dense grid.
+// The tests hold it to the reference's f64 GELU on a dense grid.
 #pragma once
 
 namespace mpc {

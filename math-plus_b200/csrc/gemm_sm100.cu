@@ -81,7 +81,7 @@ struct Cfg {
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert(!(KIND == kTF32x3 && B_MN), "3xTF32 operands are always K-major");
 };
 
@@ -121,10 +121,21 @@ __device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], i
     for (int j = 0; j < 32; ++j) f[j] *= p.alpha;
   }
   if (p.epilogue & MPC_EPI_BIAS) {
-    const int c = col0 + lane;
-    const float bl = c < p.N ? __ldg(p.bias + c) : 0.0f;
+    // Every lane adds the same 32 bias values: uniform 16-byte loads (one broadcast each) when the
+    // chunk is whole and aligned, else one load per lane and shuffles.
+    if (col0 + 32 <= p.N && !(reinterpret_cast<uintptr_t>(p.bias + col0) & 15)) {
+      const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + col0);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] += __shfl_sync(0xffffffffu, bl, j);
+      for (int j = 0; j < 8; ++j) {
+        const float4 bv = __ldg(b4 + j);
+        f[4 * j] += bv.x, f[4 * j + 1] += bv.y, f[4 * j + 2] += bv.z, f[4 * j + 3] += bv.w;
+      }
+    } else {
+      const int c = col0 + lane;
+      const float bl = c < p.N ? __ldg(p.bias + c) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] += __shfl_sync(0xffffffffu, bl, j);
+    }
   }
   if (p.epilogue & MPC_EPI_GELU) {
 #pragma unroll
@@ -590,6 +601,8 @@ static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, c
   pr.tf32 = d->dtype_in == MPC_F32;
   pr.b_mn = !pr.tf32 && d->b_layout == MPC_B_KN;
   pr.BN = pr.tf32 ? 128 : 256;
+  // 3xTF32 on a problem with fewer 128 x 128 tiles than SMs: 128 x 64 tiles keep more SMs busy.
+  if (pr.tf32 && pr.batch * ((M + 127) / 128) * ((N + 127) / 128) < dev->prop.multiProcessorCount) pr.BN = 64;
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
@@ -644,8 +657,8 @@ static int operand_maps(mpc_device *dev, const mpc_gemm_desc *d, const Prep &pr,
     const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     if ((rc = make_map_3d(&maps.a, f32, s.a.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
         (rc = make_map_3d(&maps.a_lo, f32, s.a2.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
-        (rc = make_map_3d(&maps.b, f32, s.b.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)) ||
-        (rc = make_map_3d(&maps.b_lo, f32, s.b2.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)))
+        (rc = make_map_3d(&maps.b, f32, s.b.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, pr.BN, SW)) ||
+        (rc = make_map_3d(&maps.b_lo, f32, s.b2.ptr, K, N, nB, ldk * 4, N * ldk * 4, 32, pr.BN, SW)))
       return rc;
     return MPC_OK;
   }
@@ -722,7 +735,9 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
                         128 / (uint32_t)eo, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st))) return rc;
-  if (pr.tf32)
+  if (pr.tf32 && pr.BN == 64)
+    rc = launch<kTF32x3, false, 64, 4>(dev, maps, p, st);
+  else if (pr.tf32)
     rc = launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
   else if (pr.b_mn)
     rc = launch<kHalf, true, 256, 4>(dev, maps, p, st);
