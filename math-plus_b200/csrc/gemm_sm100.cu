@@ -139,7 +139,7 @@ __device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], i
   }
   if (p.epilogue & MPC_EPI_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = gelu_erf_f32(f[j]);
+    for (int j = 0; j < 32; j += 2) gelu_erf_f32x2(f[j], f[j + 1]);
   }
 }
 
