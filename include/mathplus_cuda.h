@@ -176,6 +176,17 @@ typedef struct {
 } mpc_sdpa_desc;
 int mpc_sdpa(mpc_device *dev, const mpc_sdpa_desc *desc, const void *Q, const void *K, const void *V,
              const void *mask, void *O, float *LSE, mpc_stream s);
+/* mpc_sdpa over strided Q / K / V / O: element strides of the (batch, head, row) axes, the head-dim
+ * axis contiguous. It reads a packed projection [B, L, 3, H, D] in place (Q = base, K = base + H*D,
+ * V = base + 2*H*D, each with strides (3*L*H*D, D, 3*H*D)) and writes O as [B, L, H, D]
+ * (strides (L*H*D, D, H*D)), the layout of MultiheadAttention before out_proj
+ * (packages/tensor-autograd/src/transformer.ts:223-241), with no head split / merge copies.
+ * The tensor-core path needs every stride times 2 bytes to be a multiple of 16. */
+typedef struct {
+  int64_t q[3], k[3], v[3], o[3];
+} mpc_sdpa_layout;
+int mpc_sdpa_strided(mpc_device *dev, const mpc_sdpa_desc *desc, const void *Q, const void *K, const void *V,
+                     const void *mask, void *O, float *LSE, const mpc_sdpa_layout *layout, mpc_stream s);
 
 /* ---- the element-wise / row ops the GEMM and attention path touches ------------------------ */
 /* softmax along the middle axis of a contiguous [outer, dim, inner] block, f32 out

@@ -126,9 +126,12 @@ __device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], i
     if (col0 + 32 <= p.N && !(reinterpret_cast<uintptr_t>(p.bias + col0) & 15)) {
       const float4 *b4 = reinterpret_cast<const float4 *>(p.bias + col0);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < 8; ++j) {  // paired f32 adds
+        using namespace gelu_detail;
         const float4 bv = __ldg(b4 + j);
-        f[4 * j] += bv.x, f[4 * j + 1] += bv.y, f[4 * j + 2] += bv.z, f[4 * j + 3] += bv.w;
+        const float2 s0 = unpk(add2(pk(f[4 * j], f[4 * j + 1]), pk(bv.x, bv.y)));
+        const float2 s1 = unpk(add2(pk(f[4 * j + 2], f[4 * j + 3]), pk(bv.z, bv.w)));
+        f[4 * j] = s0.x, f[4 * j + 1] = s0.y, f[4 * j + 2] = s1.x, f[4 * j + 3] = s1.y;
       }
     } else {
       const int c = col0 + lane;

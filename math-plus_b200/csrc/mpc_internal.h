@@ -105,6 +105,9 @@ EncodeTiledFn encode_tiled();
 // Builds a 3-D tiled map over a row-major [d2][d1][d0] tensor (d0 contiguous). Strides in bytes.
 int make_map_3d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t d0, uint64_t d1, uint64_t d2,
                 uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swz);
+// A 4-D tiled map over [d3][d2][d1][d0] (d0 contiguous) with byte strides of axes 1..3.
+int make_map_4d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, const uint64_t dims[4],
+                const uint64_t strides_bytes[3], const uint32_t box[4], CUtensorMapSwizzle swz);
 
 inline size_t dtype_size(int dt) {
   switch (dt) {
@@ -125,7 +128,7 @@ inline size_t dtype_size(int dt) {
 int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, void *C, const float *bias,
              const void *resid, cudaStream_t st);
 int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void *K, const void *V, const void *mask,
-             void *O, float *LSE, cudaStream_t st);
+             void *O, float *LSE, const mpc_sdpa_layout *layout, cudaStream_t st);
 int wait_probe_run(mpc_device *dev, uint64_t timeout_ns, cudaStream_t st);
 // The product stored into `ndst` row-major matrices (pitch ldc, columns col_offset..+N-1).
 int gemm_run_multi(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, const float *bias,

@@ -121,6 +121,25 @@ int make_map_3d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint
   return MPC_OK;
 }
 
+int make_map_4d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, const uint64_t dims[4],
+                const uint64_t strides_bytes[3], const uint32_t box_dims[4], CUtensorMapSwizzle swz) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return fail(MPC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  cuuint64_t st[3] = {strides_bytes[0], strides_bytes[1], strides_bytes[2]};
+  cuuint32_t box[4] = {box_dims[0], box_dims[1], box_dims[2], box_dims[3]};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, dt, 4, const_cast<void *>(base), d, st, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MPC_ERR_INVALID,
+                "cuTensorMapEncodeTiled failed (%d): base %p dims {%llu,%llu,%llu,%llu} strides {%llu,%llu,%llu}",
+                (int)r, base, (unsigned long long)d[0], (unsigned long long)d[1], (unsigned long long)d[2],
+                (unsigned long long)d[3], (unsigned long long)st[0], (unsigned long long)st[1],
+                (unsigned long long)st[2]);
+  return MPC_OK;
+}
+
 // A single thread waits on an mbarrier that nothing ever arrives on. Its bounded wait runs out,
 // records kErrWaitProbe in the device error word and returns: the failure path every pipeline
 // wait of the GEMM and attention kernels takes, exercised without any fault.
@@ -512,7 +531,15 @@ int mpc_sdpa(mpc_device *dev, const mpc_sdpa_desc *desc, const void *Q, const vo
   int rc = enter(dev);
   if (rc) return rc;
   if (!desc) return fail(MPC_ERR_INVALID, "mpc_sdpa: null descriptor");
-  return sdpa_run(dev, desc, Q, K, V, mask, O, LSE, stream_of(dev, s));
+  return sdpa_run(dev, desc, Q, K, V, mask, O, LSE, nullptr, stream_of(dev, s));
+}
+
+int mpc_sdpa_strided(mpc_device *dev, const mpc_sdpa_desc *desc, const void *Q, const void *K, const void *V,
+                     const void *mask, void *O, float *LSE, const mpc_sdpa_layout *layout, mpc_stream s) {
+  int rc = enter(dev);
+  if (rc) return rc;
+  if (!desc || !layout) return fail(MPC_ERR_INVALID, "mpc_sdpa_strided: null descriptor or layout");
+  return sdpa_run(dev, desc, Q, K, V, mask, O, LSE, layout, stream_of(dev, s));
 }
 
 }  // extern "C"

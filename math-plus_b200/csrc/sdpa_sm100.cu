@@ -21,6 +21,7 @@
 //   TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
 // Generic path (any head dim <= 256, f32 / f16 / bf16, any alignment): one warp per query row on the
 // CUDA cores, online softmax in f32 — the role of backend-webgpu's generic sdpa kernel.
+#include <algorithm>
 #include <cfloat>
 
 #include "mpc_internal.h"
@@ -40,8 +41,10 @@ struct Params {
   const void *mask;
   long long ms[4];
   void *out;
+  long long os[3];  // element strides of O's (batch, head, row) axes
   float *lse;
   int dtype;
+  int q_pos, k_pos, v_pos;  // map axis (1..3) of head, row, batch: bits 0-1, 2-3, 4-5
   uint32_t idesc_qk, idesc_pv;
   int *err;
   unsigned long long timeout_ns;
@@ -77,7 +80,7 @@ __device__ __forceinline__ float mask_add(const Params &p, int b, int h, int q, 
 
 // One unit of work: 256 query rows (two 128-row Q tiles) of one (batch, head).
 struct Unit {
-  int bh, b, h, kvh, q0;
+  int bh, b, h, kvh, q0;  // kvh: the K/V head within the batch entry
   bool valid1;
   int last0, last1, n_kv;
 };
@@ -95,13 +98,24 @@ __device__ __forceinline__ bool unit_of(const Params &p, int k, Unit &w) {
   const int qb = (r & 1) ? (r >> 1) : qbn - 1 - (r >> 1);
   w.b = w.bh / p.H;
   w.h = w.bh - w.b * p.H;
-  w.kvh = w.b * p.Hk + w.h / p.rep;
+  w.kvh = w.h / p.rep;
   w.q0 = qb * 256;
   w.valid1 = w.q0 + 128 < p.Lq;
   w.last0 = last_kv(p, w.q0);
   w.last1 = w.valid1 ? last_kv(p, w.q0 + 128) : -1;
   w.n_kv = max(w.last0, w.last1) + 1;
   return true;
+}
+
+// One 128-row tile of a Q / K / V map: the map's outer axes are (head, row, batch) in the order
+// `pos` gives (sorted by stride on the host).
+__device__ __forceinline__ void load_rows(const CUtensorMap *map, uint64_t *bar, void *dst, int col, int head, int row,
+                                          int batch, int pos) {
+  const int ph = pos & 3, pr = (pos >> 2) & 3;
+  const int c1 = ph == 1 ? head : pr == 1 ? row : batch;
+  const int c2 = ph == 2 ? head : pr == 2 ? row : batch;
+  const int c3 = ph == 3 ? head : pr == 3 ? row : batch;
+  tma_load_4d(map, bar, dst, col, c1, c2, c3);
 }
 
 template <int D>
@@ -176,7 +190,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
         mbar_expect_tx(q_full, nq * C::TILE);
         for (int t = 0; t < nq; ++t)
           for (int s = 0; s < C::NSUB; ++s)
-            tma_load_3d(&maps.q, q_full, sq + t * C::TILE + s * C::SUB, s * 64, w.q0 + 128 * t, w.bh);
+            load_rows(&maps.q, q_full, sq + t * C::TILE + s * C::SUB, s * 64, w.h, w.q0 + 128 * t, w.b, p.q_pos);
         ++q_loads;
         for (int i = 0; i < 2 * w.n_kv; ++i, ++ring) {
           const int slot = ring % C::SLOTS;
@@ -186,7 +200,8 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
           const CUtensorMap *map = (i & 1) ? &maps.v : &maps.k;
           mbar_expect_tx(&kv_full[slot], C::TILE);
           for (int s = 0; s < C::NSUB; ++s)
-            tma_load_3d(map, &kv_full[slot], skv + slot * C::TILE + s * C::SUB, s * 64, (i >> 1) * 128, w.kvh);
+            load_rows(map, &kv_full[slot], skv + slot * C::TILE + s * C::SUB, s * 64, w.kvh, (i >> 1) * 128, w.b,
+                      (i & 1) ? p.v_pos : p.k_pos);
         }
       }
       if (!ok) {  // let the copies in flight land before shared memory is released
@@ -403,7 +418,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
         pv_cnt += last + 1;
         tc_fence_after();
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        const size_t orow = ((size_t)w.bh * p.Lq + (size_t)q) * D;
+        const size_t orow = (size_t)w.b * p.os[0] + (size_t)w.h * p.os[1] + (size_t)q * p.os[2];
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t r[32];
@@ -471,6 +486,7 @@ struct GenericParams {
   float scale;
   const void *q, *k, *v, *mask;
   long long ms[4];
+  long long qs[3], ks[3], vs[3], os[3];  // element strides of (batch, head, row)
   void *out;
   float *lse;
 };
@@ -484,8 +500,11 @@ __global__ void attn_generic_kernel(const GenericParams p) {
   const int q = (int)(row_id % p.Lq);
   const int bh = (int)(row_id / p.Lq);
   const int b = bh / p.H, h = bh % p.H;
-  const int kvh = b * p.Hk + h / p.rep;
-  for (int d = lane; d < p.D; d += 32) qs[w][d] = ld(p.q, p.dtype, (size_t)row_id * p.D + d);
+  const int kvh = h / p.rep;
+  const size_t qrow = (size_t)b * p.qs[0] + (size_t)h * p.qs[1] + (size_t)q * p.qs[2];
+  const size_t kbase = (size_t)b * p.ks[0] + (size_t)kvh * p.ks[1];
+  const size_t vbase = (size_t)b * p.vs[0] + (size_t)kvh * p.vs[1];
+  for (int d = lane; d < p.D; d += 32) qs[w][d] = ld(p.q, p.dtype, qrow + d);
   __syncwarp();
   float m = -INFINITY, l = 0.0f;
   float o[8];  // dims lane, lane+32, ..., Dv <= 256
@@ -497,7 +516,7 @@ __global__ void attn_generic_kernel(const GenericParams p) {
     float s = -INFINITY;
     if (k < k_end) {
       float acc = 0.0f;
-      const size_t kb = ((size_t)kvh * p.Lk + k) * p.D;
+      const size_t kb = kbase + (size_t)k * p.ks[2];
       for (int d = 0; d < p.D; ++d) acc = fmaf(qs[w][d], ld(p.k, p.dtype, kb + d), acc);
       s = acc * p.scale;
       if (p.mask_kind != MPC_MASK_NONE) {
@@ -525,7 +544,7 @@ __global__ void attn_generic_kernel(const GenericParams p) {
     for (int jj = 0; jj < nk; ++jj) {
       const float pj = __shfl_sync(0xffffffffu, pk, jj);
       if (pj == 0.0f) continue;  // masked keys contribute nothing (even a non-finite V row)
-      const size_t vb = ((size_t)kvh * p.Lk + k0 + jj) * p.Dv;
+      const size_t vb = vbase + (size_t)(k0 + jj) * p.vs[2];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int d = lane + 32 * i;
@@ -538,7 +557,7 @@ __global__ void attn_generic_kernel(const GenericParams p) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int d = lane + 32 * i;
-    if (d < p.Dv) st(p.out, p.dtype, (size_t)row_id * p.Dv + d, o[i] * inv);
+    if (d < p.Dv) st(p.out, p.dtype, (size_t)b * p.os[0] + (size_t)h * p.os[1] + (size_t)q * p.os[2] + d, o[i] * inv);
   }
   if (p.lse && lane == 0) p.lse[row_id] = l > 0.0f ? m + logf(l) : -INFINITY;
 }
@@ -568,8 +587,36 @@ int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t s
 
 }  // namespace attn
 
+namespace attn {
+// A 4-D map over one of Q / K / V: axes (head-dim, then head / row / batch sorted by stride so the
+// map's strides increase); the box is 64 columns x 128 rows. *pos receives each logical axis's map
+// position (head bits 0-1, row bits 2-3, batch bits 4-5).
+static int rows_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, int64_t d, int64_t heads,
+                    int64_t rows, int64_t batch, const int64_t st[3], int *pos) {
+  struct Ax {
+    int64_t extent, stride;
+    int logical;  // 0 head, 1 row, 2 batch
+  } ax[3] = {{heads, st[1], 0}, {rows, st[2], 1}, {batch, st[0], 2}};
+  int64_t top = d;
+  for (auto &a : ax) top = std::max(top, a.stride * a.extent);
+  for (auto &a : ax)
+    if (a.extent == 1) a.stride = top;  // a unit axis never moves: any valid stride
+  std::sort(ax, ax + 3, [](const Ax &x, const Ax &y) { return x.stride < y.stride; });
+  uint64_t dims[4] = {(uint64_t)d, 0, 0, 0}, strides[3];
+  uint32_t box[4] = {64, 1, 1, 1};
+  *pos = 0;
+  for (int i = 0; i < 3; ++i) {
+    dims[i + 1] = (uint64_t)ax[i].extent;
+    strides[i] = (uint64_t)ax[i].stride * 2;
+    if (ax[i].logical == 1) box[i + 1] = 128;
+    *pos |= (i + 1) << (2 * ax[i].logical);
+  }
+  return make_map_4d(map, dt, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+}  // namespace attn
+
 int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void *K, const void *V, const void *mask,
-             void *O, float *LSE, cudaStream_t st) {
+             void *O, float *LSE, const mpc_sdpa_layout *layout, cudaStream_t st) {
   using namespace attn;
   if (d->b < 0 || d->h <= 0 || d->hk <= 0 || d->lq < 0 || d->lk < 0 || d->d <= 0 || d->dv <= 0)
     return fail(MPC_ERR_INVALID, "mpc_sdpa: bad extents b=%lld h=%lld hk=%lld lq=%lld lk=%lld d=%lld dv=%lld",
@@ -585,8 +632,25 @@ int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void 
   if (!Q || !K || !V || !O) return fail(MPC_ERR_INVALID, "mpc_sdpa: null operand");
   if (d->b * d->h > (1 << 30) || d->lq > (1 << 30) || d->lk > (1 << 30))
     return fail(MPC_ERR_UNSUPPORTED, "mpc_sdpa: extents above 2^30");
+  mpc_sdpa_layout lay;
+  if (layout) {
+    lay = *layout;
+    for (const int64_t *v : {lay.q, lay.k, lay.v, lay.o})
+      for (int i = 0; i < 3; ++i)
+        if (v[i] < 0) return fail(MPC_ERR_INVALID, "mpc_sdpa_strided: negative stride");
+  } else {  // contiguous [B, H, L, D]
+    const int64_t q[3] = {d->h * d->lq * d->d, d->lq * d->d, d->d};
+    const int64_t k[3] = {d->hk * d->lk * d->d, d->lk * d->d, d->d};
+    const int64_t v[3] = {d->hk * d->lk * d->dv, d->lk * d->dv, d->dv};
+    const int64_t o[3] = {d->h * d->lq * d->dv, d->lq * d->dv, d->dv};
+    for (int i = 0; i < 3; ++i) lay.q[i] = q[i], lay.k[i] = k[i], lay.v[i] = v[i], lay.o[i] = o[i];
+  }
+  bool strides16 = true;
+  for (const int64_t *v : {lay.q, lay.k, lay.v, lay.o})
+    for (int i = 0; i < 3; ++i) strides16 = strides16 && (v[i] * 2) % 16 == 0;
   const bool aligned = !((uintptr_t)Q & 15) && !((uintptr_t)K & 15) && !((uintptr_t)V & 15) && !((uintptr_t)O & 15);
-  const bool tc = d->dtype != MPC_F32 && d->d == d->dv && (d->d == 64 || d->d == 128) && aligned && d->lk > 0;
+  const bool tc = d->dtype != MPC_F32 && d->d == d->dv && (d->d == 64 || d->d == 128) && aligned && strides16 &&
+                  d->lk > 0;
   if (!tc) {
     if (d->d > 256 || d->dv > 256) return fail(MPC_ERR_UNSUPPORTED, "mpc_sdpa: head dim above 256");
     GenericParams g{};
@@ -594,6 +658,7 @@ int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void 
     g.Dv = (int)d->dv, g.rep = (int)(d->h / d->hk), g.causal = d->causal ? 1 : 0, g.dtype = d->dtype;
     g.mask_kind = d->mask_kind, g.scale = d->scale, g.q = Q, g.k = K, g.v = V, g.mask = mask, g.out = O, g.lse = LSE;
     for (int i = 0; i < 4; ++i) g.ms[i] = d->mask_strides[i];
+    for (int i = 0; i < 3; ++i) g.qs[i] = lay.q[i], g.ks[i] = lay.k[i], g.vs[i] = lay.v[i], g.os[i] = lay.o[i];
     const long long rows = d->b * d->h * d->lq;
     attn_generic_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(g);
     dev->launches++;
@@ -613,6 +678,7 @@ int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void 
   p.mask = mask;
   for (int i = 0; i < 4; ++i) p.ms[i] = d->mask_strides[i];
   p.out = O;
+  for (int i = 0; i < 3; ++i) p.os[i] = lay.o[i];
   p.lse = LSE;
   p.dtype = d->dtype;
   const uint32_t fmt = d->dtype == MPC_BF16 ? kFmtBF16 : kFmtF16;
@@ -623,15 +689,13 @@ int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void 
   Maps maps;
   memset(&maps, 0, sizeof(maps));
   const CUtensorMapDataType dt = d->dtype == MPC_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const uint64_t rowb = (uint64_t)p.D * 2;
-  int rc;
-  if ((rc = make_map_3d(&maps.q, dt, Q, p.D, p.Lq, (uint64_t)p.B * p.H, rowb, rowb * p.Lq, 64, 128,
-                        CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_map_3d(&maps.k, dt, K, p.D, p.Lk, (uint64_t)p.B * p.Hk, rowb, rowb * p.Lk, 64, 128,
-                        CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_map_3d(&maps.v, dt, V, p.D, p.Lk, (uint64_t)p.B * p.Hk, rowb, rowb * p.Lk, 64, 128,
-                        CU_TENSOR_MAP_SWIZZLE_128B)))
+  int rc, kpos = 0, vpos = 0;
+  if ((rc = rows_map(&maps.q, dt, Q, p.D, p.H, p.Lq, p.B, lay.q, &p.q_pos)) ||
+      (rc = rows_map(&maps.k, dt, K, p.D, p.Hk, p.Lk, p.B, lay.k, &kpos)) ||
+      (rc = rows_map(&maps.v, dt, V, p.D, p.Hk, p.Lk, p.B, lay.v, &vpos)))
     return rc;
+  p.k_pos = kpos;
+  p.v_pos = vpos;
   return p.D == 128 ? launch_tc<128>(dev, maps, p, st) : launch_tc<64>(dev, maps, p, st);
 }
 

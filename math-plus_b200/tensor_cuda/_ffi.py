@@ -40,6 +40,11 @@ class DeviceInfo(C.Structure):
                 ("runtime_version", C.c_int), ("driver_version", C.c_int)]
 
 
+class SdpaLayout(C.Structure):
+    """mpc_sdpa_layout: element strides of (batch, head, row) for Q, K, V and O."""
+    _fields_ = [("q", C.c_int64 * 3), ("k", C.c_int64 * 3), ("v", C.c_int64 * 3), ("o", C.c_int64 * 3)]
+
+
 class GemmDesc(C.Structure):
     _fields_ = [("m", C.c_int64), ("n", C.c_int64), ("k", C.c_int64), ("dtype_in", C.c_int32),
                 ("dtype_out", C.c_int32), ("b_layout", C.c_int32), ("epilogue", C.c_int32), ("alpha", C.c_float),
@@ -90,6 +95,7 @@ SIGNATURES = {
     "mpc_sync": [_dev],
     "mpc_launch_count": [_dev, C.POINTER(_u64)],
     "mpc_gemm": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
+    "mpc_sdpa_strided": [_dev, C.POINTER(SdpaDesc), _vp, _vp, _vp, _vp, _vp, _vp, C.POINTER(SdpaLayout), _vp],
     "mpc_gemm_residual": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp, _vp],
     "mpc_gemm_f32_noalloc": [C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
     "mpc_sdpa": [_dev, C.POINTER(SdpaDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp],

@@ -494,6 +494,31 @@ class CudaBackend:
                          lse_t._buf.ptr if lse_t is not None else None)
         return (out, lse_t) if lse else out
 
+    def sdpa_packed(self, qkv: CudaTensor, n_head: int, scale: float, causal: bool = False) -> CudaTensor:
+        """Self-attention over a packed projection, as ``MultiheadAttention`` does it
+        (packages/tensor-autograd/src/transformer.ts:223-241): ``qkv`` [B, L, 3·H·Dh] laid out
+        [B, L, 3, H, Dh] (the in-projection's output) -> [B, L, H·Dh] with heads merged, read and
+        written in place by one kernel (no head split / merge copies)."""
+        self._check_live(qkv)
+        if len(qkv.shape) != 3 or qkv.shape[2] % (3 * n_head):
+            raise ValueError(f"tensor-cuda: sdpa_packed: qkv [{','.join(map(str, qkv.shape))}] for {n_head} heads")
+        if qkv.dtype not in FLOAT:
+            raise TypeError("tensor-cuda: sdpa_packed: float dtypes only")
+        B, L, three_e = qkv.shape
+        E = three_e // 3
+        Dh = E // n_head
+        out = self._alloc((B, L, E), qkv.dtype)
+        base = qkv.ptr
+        eb = F.DTYPE_BYTES[F.DTYPE_CODES[qkv.dtype]]
+        lay = F.SdpaLayout()
+        for name in ("q", "k", "v"):
+            getattr(lay, name)[:] = [L * three_e, Dh, three_e]
+        lay.o[:] = [L * E, Dh, E]
+        desc = sdpa_desc(B, n_head, n_head, L, L, Dh, Dh, F.DTYPE_CODES[qkv.dtype], causal, scale)
+        F.call("mpc_sdpa_strided", self.device.handle, C.byref(desc), C.c_void_p(base), C.c_void_p(base + E * eb),
+               C.c_void_p(base + 2 * E * eb), None, C.c_void_p(out._buf.ptr), None, C.byref(lay), None)
+        return out
+
     def layerNorm(self, x: CudaTensor, weight: CudaTensor | None, bias: CudaTensor | None, eps: float = 1e-5):
         self._check_live(x, weight, bias)
         d = x.shape[-1]

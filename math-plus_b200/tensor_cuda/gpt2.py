@@ -9,9 +9,9 @@ The block is the reference's pre-norm transformer layer (``TransformerEncoderLay
 embeddings lead in and a final LayerNorm and the tied LM head (``linear`` with the token table)
 lead out.
 
-Every step is one device op: ``embedding``, ``add``, ``layerNorm``, ``linear`` (bias, and GELU for
-the first MLP projection, in the GEMM's epilogue), ``transpose`` (head split / merge), ``split``
-(views), ``sdpa`` (causal, fused). Activations and weight matrices are bf16; biases and LayerNorm
+Every step is one device op: ``embedding``, ``add``, ``layerNorm``, ``linear`` (bias, GELU for the
+first MLP projection and the residual adds in the GEMM's epilogue) and ``sdpa_packed`` (causal
+attention reading Q / K / V straight from the packed in-projection and writing the heads merged). Activations and weight matrices are bf16; biases and LayerNorm
 parameters f32; every GEMM accumulates in f32.
 """
 from __future__ import annotations
@@ -123,17 +123,12 @@ class GPT2:
         tmp = []
         h = be.layerNorm(x, w[p + "ln_1.weight"], w[p + "ln_1.bias"], eps)
         qkv = be.linear(h, w[p + "attn.in_proj_weight"], w[p + "attn.in_proj_bias"])      # [B*L, 3D]
-        qkv5 = be.reshape(qkv, (B, L, 3, H, Dh))
-        heads = be.transpose(qkv5, (2, 0, 3, 1, 4))                                       # [3, B, H, L, Dh]
-        parts = be.split(heads, 3, 0)
-        q, k, v = (be.reshape(t, (B, H, L, Dh)) for t in parts)
-        tmp += [h, qkv, qkv5, heads, *parts, q, k, v]
-        a = be.sdpa(q, k, v, None, 1.0 / math.sqrt(Dh), causal=True)                     # [B, H, L, Dh]
-        at = be.transpose(a, (0, 2, 1, 3))                                                # [B, L, H, Dh]
-        merged = be.reshape(at, (B * L, D))
+        qkv3 = be.reshape(qkv, (B, L, 3 * D))                                              # [B, L, 3, H, Dh]
+        a = be.sdpa_packed(qkv3, H, 1.0 / math.sqrt(Dh), causal=True)                     # [B, L, H*Dh]
+        merged = be.reshape(a, (B * L, D))
         o = be.linear(merged, w[p + "attn.out_proj.weight"], w[p + "attn.out_proj.bias"])
         x1 = be.add(x, o)
-        tmp += [a, at, merged, o]
+        tmp += [h, qkv, qkv3, a, merged, o]
         h2 = be.layerNorm(x1, w[p + "ln_2.weight"], w[p + "ln_2.bias"], eps)
         f = be.linear(h2, w[p + "mlp.fc.weight"], w[p + "mlp.fc.bias"], activation="gelu")  # [B*L, d_ff]
         g = be.linear(f, w[p + "mlp.proj.weight"], w[p + "mlp.proj.bias"])

@@ -186,3 +186,30 @@ def test_causal_attention_full_config_sampled(dev):
                       v[b:b + 1, h:h + 1].astype(np.float32), mask, 1 / np.sqrt(D), threads=O.default_threads())
         g = got[b:b + 1, h:h + 1]
         assert np.all(np.abs(g - want) <= 2e-3 + 1e-2 * np.abs(want)), (b, h, np.abs(g - want).max())
+
+
+@pytest.mark.parametrize("dtype,D,causal", [("bf16", 64, True), ("f16", 128, False), ("f32", 64, True)])
+def test_packed_qkv_layout_matches_the_contiguous_oracle(dev, dtype, D, causal):
+    """mpc_sdpa_strided on a packed [B, L, 3, H, D] projection writing [B, L, H, D] (the tensor-core
+    path for f16 / bf16, the CUDA-core path for f32) against the oracle on the split heads."""
+    from tensor_cuda import _ffi as F
+    from tensor_cuda.backend import CudaBackend, host
+    B, L, H = 2, 300, 3
+    x = exact(O.normal_f32(B * L * 3 * H * D, 61).reshape(B, L, 3, H, D), dtype)
+    be = CudaBackend(dev)
+    if dtype == "bf16":
+        bits = (x.astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+        t = be.from_host_sync(host("bf16", (B, L, 3 * H * D), bits))
+    else:
+        t = be.from_host_sync(host(dtype, (B, L, 3 * H * D), x.reshape(B, L, -1)))
+    out = be.read_sync(be.sdpa_packed(t, H, 1 / np.sqrt(D), causal=causal))
+    got = out.data
+    if dtype == "bf16":
+        got = (got.astype(np.uint32) << 16).view(np.float32)
+    got = np.asarray(got, np.float32).reshape(B, L, H, D)
+    q, k, v = (np.ascontiguousarray(np.transpose(x[:, :, i].astype(np.float32), (0, 2, 1, 3))) for i in range(3))
+    mask = np.tril(np.ones((L, L), np.bool_)).reshape(1, 1, L, L) if causal else None
+    want = np.transpose(O.sdpa(q, k, v, mask, 1 / np.sqrt(D), threads=O.default_threads()), (0, 2, 1, 3))
+    tol = {"f32": 1e-5 + 1e-5 * np.abs(want), "f16": 2e-3 + 1e-2 * np.abs(want),
+           "bf16": 1e-2 + 2e-2 * np.abs(want)}[dtype]
+    assert np.all(np.abs(got - want) <= tol), np.abs(got - want).max()
