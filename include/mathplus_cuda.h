@@ -217,6 +217,40 @@ int mpc_cast(mpc_device *dev, const void *x, int32_t dtype_in, void *out, int32_
 int mpc_transpose(mpc_device *dev, const void *x, void *out, int32_t elem_bytes, int32_t rank, const int64_t *shape,
                   const int32_t *perm, mpc_stream s);
 
+/* ---- the rest of the Backend op set (CpuBackendImpl, packages/tensor-cpu/src/index.ts:560-735) --
+ * Arithmetic in f64 (every stored type widens exactly), one rounding on store. Operand
+ * strides are element strides aligned to the output shape, 0 on broadcast axes (at most 6 axes).
+ * Comparison and logical results are bool (u8 0 / 1); argmax / argmin write i32. */
+enum {
+  MPC_OP_NEG = 1, MPC_OP_ABS, MPC_OP_EXP, MPC_OP_LOG, MPC_OP_SQRT, MPC_OP_RSQRT, MPC_OP_TANH, MPC_OP_SIGMOID,
+  MPC_OP_RELU, MPC_OP_ERF, MPC_OP_SCALE, MPC_OP_POW_SCALAR, MPC_OP_LOGICAL_NOT,           /* unary */
+  MPC_OP_ADD = 32, MPC_OP_SUB, MPC_OP_MUL, MPC_OP_DIV, MPC_OP_MAXIMUM, MPC_OP_POW, MPC_OP_EQUAL,
+  MPC_OP_NOT_EQUAL, MPC_OP_LESS, MPC_OP_LESS_EQUAL, MPC_OP_GREATER, MPC_OP_GREATER_EQUAL,
+  MPC_OP_LOGICAL_AND, MPC_OP_LOGICAL_OR,                                                  /* binary */
+  MPC_OP_SUM = 64, MPC_OP_MEAN, MPC_OP_MAX, MPC_OP_MIN, MPC_OP_ARGMAX, MPC_OP_ARGMIN     /* reductions */
+};
+/* out[i] = op(x[i]) (alpha: the factor of SCALE, the exponent of POW_SCALAR). */
+int mpc_unary(mpc_device *dev, int32_t op, const void *x, int32_t dtype_in, void *out, int32_t dtype_out, int64_t n,
+              float alpha, mpc_stream s);
+/* out = op(x, y) over shape[rank] with broadcast strides. */
+int mpc_binary(mpc_device *dev, int32_t op, const void *x, const void *y, int32_t dtype_in, void *out,
+               int32_t dtype_out, int32_t rank, const int64_t *shape, const int64_t *x_strides,
+               const int64_t *y_strides, mpc_stream s);
+/* out = cond ? x : y (Backend.where), cond bool. */
+int mpc_where(mpc_device *dev, const uint8_t *cond, const void *x, const void *y, int32_t dtype, void *out,
+              int32_t rank, const int64_t *shape, const int64_t *c_strides, const int64_t *x_strides,
+              const int64_t *y_strides, mpc_stream s);
+/* Reduction of the middle axis of a contiguous [outer, dim, inner] (Backend.sum / mean / max / min /
+ * argmax / argmin, kernels.ts:125-187, :543-568), out [outer, inner]. */
+int mpc_reduce(mpc_device *dev, int32_t op, const void *x, int32_t dtype_in, void *out, int32_t dtype_out,
+               int64_t outer, int64_t dim, int64_t inner, mpc_stream s);
+/* Inclusive prefix sum along the middle axis (Backend.cumsum, kernels.ts:577-592). */
+int mpc_cumsum(mpc_device *dev, const void *x, int32_t dtype_in, void *out, int32_t dtype_out, int64_t outer,
+               int64_t dim, int64_t inner, mpc_stream s);
+/* out[Σ i_k·out_strides_k] = x[Σ i_k·x_strides_k] over shape[rank]: slice, concat, broadcast copies. */
+int mpc_strided_copy(mpc_device *dev, const void *x, const int64_t *x_strides, void *out, const int64_t *out_strides,
+                     int32_t elem_bytes, int32_t rank, const int64_t *shape, mpc_stream s);
+
 /* ---- multi-GPU: NCCL over NVLink, one rank per process (no reference counterpart) ---------- */
 int mpc_comm_unique_id(void *id128);
 int mpc_comm_init(mpc_device *dev, int nranks, int rank, const void *id128, mpc_comm **comm);

@@ -26,6 +26,14 @@ DTYPE_BYTES = {F32: 4, F16: 2, BF16: 2, I32: 4, BOOL: 1}
 EPI_BIAS, EPI_GELU, EPI_RESIDUAL = 1, 2, 4
 B_KN, B_NK = 0, 1
 MASK_NONE, MASK_BOOL, MASK_ADD = 0, 1, 2
+# mpc op codes (include/mathplus_cuda.h)
+UNARY_OPS = {name: i + 1 for i, name in enumerate(
+    ["neg", "abs", "exp", "log", "sqrt", "rsqrt", "tanh", "sigmoid", "relu", "erf", "scale", "pow_scalar",
+     "logicalNot"])}
+BINARY_OPS = {name: i + 32 for i, name in enumerate(
+    ["add", "sub", "mul", "div", "maximum", "pow", "equal", "notEqual", "less", "lessEqual", "greater",
+     "greaterEqual", "logicalAnd", "logicalOr"])}
+REDUCE_OPS = {name: i + 64 for i, name in enumerate(["sum", "mean", "max", "min", "argmax", "argmin"])}
 
 
 class MpcError(RuntimeError):
@@ -96,6 +104,13 @@ SIGNATURES = {
     "mpc_launch_count": [_dev, C.POINTER(_u64)],
     "mpc_gemm": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
     "mpc_sdpa_strided": [_dev, C.POINTER(SdpaDesc), _vp, _vp, _vp, _vp, _vp, _vp, C.POINTER(SdpaLayout), _vp],
+    "mpc_unary": [_dev, _i32, _vp, _i32, _vp, _i32, _i64, C.c_float, _vp],
+    "mpc_binary": [_dev, _i32, _vp, _vp, _i32, _vp, _i32, _i32, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64), _vp],
+    "mpc_where": [_dev, _vp, _vp, _vp, _i32, _vp, _i32, C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64),
+                  C.POINTER(_i64), _vp],
+    "mpc_reduce": [_dev, _i32, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _vp],
+    "mpc_cumsum": [_dev, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _vp],
+    "mpc_strided_copy": [_dev, _vp, C.POINTER(_i64), _vp, C.POINTER(_i64), _i32, _i32, C.POINTER(_i64), _vp],
     "mpc_gemm_residual": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp, _vp],
     "mpc_gemm_f32_noalloc": [C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
     "mpc_sdpa": [_dev, C.POINTER(SdpaDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp],

@@ -1,9 +1,13 @@
 """``CudaBackend``: the ``@johnhenry/tensor-backend`` ``Backend`` contract over libmathplus_cuda.so.
 
-Mirrors the method set of tensor-cpu's ``CpuBackendImpl`` (packages/tensor-cpu/src/index.ts:200-861)
-for the GEMM / attention path: transfers (``fromHost`` / ``read``, async), lifetime (``dispose``,
-``scope``, ``flush``, ``destroy``), ``reshape``, ``cast``, ``add``, ``gelu``, ``softmax``,
-``matmul``, ``linear``, ``sdpa``, ``layerNorm``, ``embedding``.
+Mirrors the method set of tensor-cpu's ``CpuBackendImpl`` (packages/tensor-cpu/src/index.ts:200-861):
+transfers (``fromHost`` / ``read``, async), lifetime (``dispose``, ``scope``, ``flush``,
+``destroy``), ``reshape``, ``transpose``, ``slice``, ``split``, ``concat``, ``cast``, the element-wise
+ops (``add``, ``sub``, ``mul``, ``div``, ``maximum``, ``pow``, ``where``, ``scale``, ``exp``, ``log``,
+``relu``, ``gelu``, ``sqrt``, ``rsqrt``, ``tanh``, ``sigmoid``, ``erf``, ``neg``, ``abs``),
+comparisons and logical ops, reductions (``sum``, ``mean``, ``max``, ``min``, ``argmax``,
+``argmin``, ``cumsum``, ``softmax``), and the contractions ``matmul``, ``linear``, ``sdpa``,
+``layerNorm``, ``embedding``.
 
 Lazy inside, eager-observable (RFC 0001 §12 Q1, as the MLX and WebGPU backends): ``matmul`` and
 ``linear`` return a handle whose GEMM has not run yet; an ``add`` of a bias row, a ``gelu`` and
@@ -409,6 +413,230 @@ class CudaBackend:
             res = self.cast(out, x.dtype)
             out._release()
             return res
+        return out
+
+    # ---- the rest of the element-wise / comparison / reduction / copy ops -----------------------
+    # (CpuBackendImpl, packages/tensor-cpu/src/index.ts:318-735): evaluated in f64 on the device
+    # with one rounding on store; same-dtype operands (no implicit promotion), broadcasting as
+    # tensor-core's broadcastShapes.
+    def _unary(self, x: CudaTensor, name: str, out_dtype: str | None = None, alpha: float = 0.0) -> CudaTensor:
+        self._check_live(x)
+        out = self._alloc(x.shape, out_dtype or x.dtype)
+        F.call("mpc_unary", self.device.handle, F.UNARY_OPS[name], C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype],
+               C.c_void_p(out._buf.ptr), F.DTYPE_CODES[out.dtype], x.size, C.c_float(alpha), None)
+        return out
+
+    def _float_out(self, x: CudaTensor) -> str:
+        return x.dtype if x.dtype in FLOAT else "f32"
+
+    def exp(self, x):
+        return self._unary(x, "exp", self._float_out(x))
+
+    def log(self, x):
+        return self._unary(x, "log", self._float_out(x))
+
+    def sqrt(self, x):
+        return self._unary(x, "sqrt", self._float_out(x))
+
+    def rsqrt(self, x):
+        return self._unary(x, "rsqrt", self._float_out(x))
+
+    def tanh(self, x):
+        return self._unary(x, "tanh", self._float_out(x))
+
+    def sigmoid(self, x):
+        return self._unary(x, "sigmoid", self._float_out(x))
+
+    def erf(self, x):
+        return self._unary(x, "erf", self._float_out(x))
+
+    def relu(self, x):
+        return self._unary(x, "relu")
+
+    def neg(self, x):
+        return self._unary(x, "neg")
+
+    def abs(self, x):
+        return self._unary(x, "abs")
+
+    def scale(self, x, s: float):
+        return self._unary(x, "scale", self._float_out(x), float(s))
+
+    def logicalNot(self, x):
+        return self._unary(x, "logicalNot", "bool")
+
+    @staticmethod
+    def _strides_arr(strides):
+        return (C.c_int64 * max(1, len(strides)))(*strides)
+
+    def _binary(self, a: CudaTensor, b: CudaTensor, name: str, out_dtype: str | None = None) -> CudaTensor:
+        self._check_live(a, b)
+        if a.dtype != b.dtype:
+            raise TypeError(f"tensor-cuda: {name}: dtype mismatch {a.dtype} vs {b.dtype} (no implicit promotion)")
+        shape = P.broadcast_shapes(a.shape, b.shape)
+        if len(shape) > 6:
+            raise NotImplementedError(f"tensor-cuda: {name}: more than 6 axes")
+        dt = out_dtype or ("i32" if a.dtype == "bool" else a.dtype)
+        out = self._alloc(shape, dt)
+        F.call("mpc_binary", self.device.handle, F.BINARY_OPS[name], C.c_void_p(a.ptr), C.c_void_p(b.ptr),
+               F.DTYPE_CODES[a.dtype], C.c_void_p(out._buf.ptr), F.DTYPE_CODES[dt], len(shape),
+               self._strides_arr(shape), self._strides_arr(P.aligned_strides(a.shape, shape)),
+               self._strides_arr(P.aligned_strides(b.shape, shape)), None)
+        return out
+
+    def sub(self, a, b):
+        return self._binary(a, b, "sub")
+
+    def mul(self, a, b):
+        return self._binary(a, b, "mul")
+
+    def div(self, a, b):
+        return self._binary(a, b, "div")
+
+    def maximum(self, a, b):
+        return self._binary(a, b, "maximum")
+
+    def pow(self, a, b):
+        if a.dtype not in FLOAT:
+            raise TypeError(f"tensor-cuda: pow: float dtypes only, got {a.dtype}")
+        return self._binary(a, b, "pow")
+
+    def equal(self, a, b):
+        return self._binary(a, b, "equal", "bool")
+
+    def notEqual(self, a, b):
+        return self._binary(a, b, "notEqual", "bool")
+
+    def less(self, a, b):
+        return self._binary(a, b, "less", "bool")
+
+    def lessEqual(self, a, b):
+        return self._binary(a, b, "lessEqual", "bool")
+
+    def greater(self, a, b):
+        return self._binary(a, b, "greater", "bool")
+
+    def greaterEqual(self, a, b):
+        return self._binary(a, b, "greaterEqual", "bool")
+
+    def logicalAnd(self, a, b):
+        return self._binary(a, b, "logicalAnd", "bool")
+
+    def logicalOr(self, a, b):
+        return self._binary(a, b, "logicalOr", "bool")
+
+    def where(self, cond: CudaTensor, a: CudaTensor, b: CudaTensor) -> CudaTensor:
+        """cond ? a : b with broadcasting (index.ts:511-545); cond is bool."""
+        self._check_live(cond, a, b)
+        if cond.dtype != "bool":
+            raise TypeError(f"tensor-cuda: where: the condition is bool, got {cond.dtype}")
+        if a.dtype != b.dtype:
+            raise TypeError(f"tensor-cuda: where: dtype mismatch {a.dtype} vs {b.dtype} (no implicit promotion)")
+        shape = P.broadcast_shapes(P.broadcast_shapes(cond.shape, a.shape), b.shape)
+        out = self._alloc(shape, a.dtype)
+        F.call("mpc_where", self.device.handle, C.c_void_p(cond.ptr), C.c_void_p(a.ptr), C.c_void_p(b.ptr),
+               F.DTYPE_CODES[a.dtype], C.c_void_p(out._buf.ptr), len(shape), self._strides_arr(shape),
+               self._strides_arr(P.aligned_strides(cond.shape, shape)),
+               self._strides_arr(P.aligned_strides(a.shape, shape)),
+               self._strides_arr(P.aligned_strides(b.shape, shape)), None)
+        return out
+
+    @staticmethod
+    def _around(shape, axis: int):
+        nd = len(shape)
+        if not -nd <= axis < nd:
+            raise ValueError(f"tensor-cuda: axis {axis} out of range for rank {nd}")
+        a = axis % nd
+        outer = int(np.prod(shape[:a])) if a else 1
+        inner = int(np.prod(shape[a + 1:])) if a + 1 < nd else 1
+        return a, outer, int(shape[a]), inner
+
+    def _reduce(self, x: CudaTensor, axis: int, keepDims: bool, name: str, dt: str) -> CudaTensor:
+        self._check_live(x)
+        a, outer, dim, inner = self._around(x.shape, axis)
+        if dim == 0 and name not in ("sum", "mean"):
+            raise ValueError(f"tensor-cuda: {name} over an empty axis")
+        shape = tuple(x.shape[:a]) + ((1,) if keepDims else ()) + tuple(x.shape[a + 1:])
+        out = self._alloc(shape, dt)
+        F.call("mpc_reduce", self.device.handle, F.REDUCE_OPS[name], C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype],
+               C.c_void_p(out._buf.ptr), F.DTYPE_CODES[dt], outer, dim, inner, None)
+        return out
+
+    def sum(self, x, axis: int, keepDims: bool = False):
+        return self._reduce(x, axis, keepDims, "sum", "i32" if x.dtype in ("bool", "i32") else x.dtype)
+
+    def mean(self, x, axis: int, keepDims: bool = False):
+        return self._reduce(x, axis, keepDims, "mean", self._float_out(x))
+
+    def max(self, x, axis: int, keepDims: bool = False):
+        return self._reduce(x, axis, keepDims, "max", x.dtype)
+
+    def min(self, x, axis: int, keepDims: bool = False):
+        return self._reduce(x, axis, keepDims, "min", x.dtype)
+
+    def argmax(self, x, axis: int, keepDims: bool = False):
+        return self._reduce(x, axis, keepDims, "argmax", "i32")
+
+    def argmin(self, x, axis: int, keepDims: bool = False):
+        return self._reduce(x, axis, keepDims, "argmin", "i32")
+
+    def cumsum(self, x: CudaTensor, axis: int) -> CudaTensor:
+        self._check_live(x)
+        _, outer, dim, inner = self._around(x.shape, axis)
+        dt = "i32" if x.dtype in ("bool", "i32") else x.dtype
+        out = self._alloc(x.shape, dt)
+        F.call("mpc_cumsum", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(out._buf.ptr),
+               F.DTYPE_CODES[dt], outer, dim, inner, None)
+        return out
+
+    def slice(self, x: CudaTensor, begin, end) -> CudaTensor:
+        """x[begin:end] per axis, negative indices from the end, clamped (index.ts:333-352)."""
+        self._check_live(x)
+        nd = len(x.shape)
+        in_st = [int(np.prod(x.shape[i + 1:])) for i in range(nd)]  # row-major strides
+        shape, base = [], 0
+        for i, d in enumerate(x.shape):
+            lo = begin[i] if i < len(begin) else 0
+            hi = end[i] if i < len(end) else d
+            lo += d if lo < 0 else 0
+            hi += d if hi < 0 else 0
+            lo = min(max(lo, 0), d)
+            hi = min(max(hi, lo), d)
+            base += lo * in_st[i]
+            shape.append(hi - lo)
+        out = self._alloc(shape, x.dtype)
+        eb = F.DTYPE_BYTES[F.DTYPE_CODES[x.dtype]]
+        out_st = [int(np.prod(shape[i + 1:])) for i in range(nd)]
+        F.call("mpc_strided_copy", self.device.handle, C.c_void_p(x.ptr + base * eb), self._strides_arr(in_st),
+               C.c_void_p(out._buf.ptr), self._strides_arr(out_st), eb, nd, self._strides_arr(shape), None)
+        return out
+
+    def concat(self, xs, axis: int) -> CudaTensor:
+        """Join along ``axis`` (index.ts:368-404); every input has the same dtype."""
+        if not xs:
+            raise ValueError("tensor-cuda: concat of nothing")
+        self._check_live(*xs)
+        first = xs[0]
+        nd = len(first.shape)
+        a = axis % nd
+        for t in xs:
+            if t.dtype != first.dtype:
+                raise TypeError(f"tensor-cuda: concat: dtype mismatch {first.dtype} vs {t.dtype} (no implicit promotion)")
+            if len(t.shape) != nd or any(t.shape[i] != first.shape[i] for i in range(nd) if i != a):
+                raise ValueError(f"tensor-cuda: concat: shapes {[list(t.shape) for t in xs]} along axis {axis}")
+        shape = list(first.shape)
+        shape[a] = sum(t.shape[a] for t in xs)
+        out = self._alloc(shape, first.dtype)
+        eb = F.DTYPE_BYTES[F.DTYPE_CODES[first.dtype]]
+        out_st = [int(np.prod(shape[i + 1:])) for i in range(nd)]
+        off = 0
+        for t in xs:
+            if t.size:
+                in_st = [int(np.prod(t.shape[i + 1:])) for i in range(nd)]
+                F.call("mpc_strided_copy", self.device.handle, C.c_void_p(t.ptr), self._strides_arr(in_st),
+                       C.c_void_p(out._buf.ptr + off * out_st[a] * eb), self._strides_arr(out_st), eb, nd,
+                       self._strides_arr(t.shape), None)
+            off += t.shape[a]
         return out
 
     # ---- contractions --------------------------------------------------------------------------
