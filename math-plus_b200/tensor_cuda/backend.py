@@ -356,8 +356,8 @@ class CudaBackend:
         self._check_live(x, y)
         if x.dtype != y.dtype:
             raise TypeError(f"tensor-cuda: add: dtype mismatch {x.dtype} vs {y.dtype} (no implicit promotion)")
-        if x.dtype not in FLOAT:
-            raise NotImplementedError("tensor-cuda: add: float dtypes only")
+        if x.dtype not in FLOAT or P.broadcast_shapes(x.shape, y.shape) not in (tuple(x.shape), tuple(y.shape)):
+            return self._binary(x, y, "add")  # integer data, or both operands broadcast
         if x.size < y.size:  # add is commutative: keep the larger operand first
             x, y = y, x
         pg = x._pending
@@ -376,7 +376,10 @@ class CudaBackend:
                     _ = r.ptr
                     folded = replace(pa, resid=r._buf, epilogue=pa.epilogue | F.EPI_RESIDUAL).retain()
                     return self._make(a.shape, a.dtype, pending=folded)
-        n_x, n_y = P.add_plan(x.shape, y.shape)
+        try:
+            n_x, n_y = P.add_plan(x.shape, y.shape)
+        except NotImplementedError:  # not a repeated trailing block: the general broadcast kernel
+            return self._binary(x, y, "add")
         out = self._alloc(x.shape, x.dtype)
         F.call("mpc_add", self.device.handle, C.c_void_p(x.ptr), C.c_void_p(y.ptr), C.c_void_p(out._buf.ptr),
                F.DTYPE_CODES[x.dtype], n_x, n_y, None)

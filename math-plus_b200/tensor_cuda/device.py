@@ -104,6 +104,16 @@ class ArrayDevice:
                     self._scopes[-1].add(a)
         return result
 
+    def where(self, cond: "DeviceArray", a: "DeviceArray", b: "DeviceArray") -> "DeviceArray":
+        """cond ? a : b, elementwise with broadcasting (device-array.ts:154-162)."""
+        c = self._own(cond, "where")
+        x, y = self._own(a, "where"), self._own(b, "where")
+        if c.dtype != "bool":
+            raise TypeError(f"{_LABEL} where: the condition must be bool, got {c.dtype}")
+        if x.dtype != y.dtype:
+            raise TypeError(f"{_LABEL} where: dtype mismatch {x.dtype} vs {y.dtype} (no implicit promotion; cast() first)")
+        return self.wrap(self.backend.where(c, x, y))
+
     def destroy(self) -> None:
         self.backend.destroy()
 
@@ -207,12 +217,179 @@ class DeviceArray:
             raise TypeError(f"{_LABEL} {op}: needs a float array, got {x.dtype}")
         return x
 
-    def add(self, other: "DeviceArray") -> "DeviceArray":
-        x = self._float("add")
-        y = self.device._own(other, "add")
+    def _check(self, op: str, kind: str) -> CudaTensor:
+        """What an op accepts: any dtype, numeric (not bool), float only, or bool only
+        (device-array.ts:486-494)."""
+        x = self._handle(op)
+        dt = x.dtype
+        if kind == "numeric" and dt == "bool":
+            raise TypeError(f"{_LABEL} {op}: not defined for bool; cast() first")
+        if kind == "float" and dt not in FLOAT:
+            raise TypeError(f"{_LABEL} {op}: needs a float dtype, got {dt}; cast(\"f32\") first (no implicit promotion)")
+        if kind == "bool" and dt != "bool":
+            raise TypeError(f"{_LABEL} {op}: needs bool operands, got {dt}; cast(\"bool\") first (no implicit truthiness)")
+        return x
+
+    def _unary(self, op: str, kind: str, f) -> "DeviceArray":
+        return self._wrap(f(self.device.backend, self._check(op, kind)))
+
+    def _binary(self, op: str, other, kind: str, f) -> "DeviceArray":
+        """A binary op; a number operand becomes an on-device constant of this array's dtype
+        (device-array.ts:503-516)."""
+        x = self._check(op, kind)
+        be = self.device.backend
+        if isinstance(other, (int, float)) and not isinstance(other, bool):
+            if kind == "bool":
+                raise TypeError(f"{_LABEL} {op}: needs a DeviceArray operand")
+            y = be.from_host_sync(host(x.dtype, (1,), [other]))
+            try:
+                return self._wrap(f(be, x, y))
+            finally:
+                be.dispose(y)
+        y = self.device._own(other, op)
         if x.dtype != y.dtype:
-            raise TypeError(f"{_LABEL} add: dtype mismatch {x.dtype} vs {y.dtype} (no implicit promotion; cast() first)")
-        return self._wrap(self.device.backend.add(x, y))
+            raise TypeError(f"{_LABEL} {op}: dtype mismatch {x.dtype} vs {y.dtype} (no implicit promotion; cast() first)")
+        return self._wrap(f(be, x, y))
+
+    def _reduce(self, op: str, kind: str, axis, keepDims: bool, f) -> "DeviceArray":
+        """One axis, or every element (through a flat view) when ``axis`` is None (:519-539)."""
+        x = self._check(op, kind)
+        be = self.device.backend
+        nd = len(x.shape)
+        if axis is not None:
+            if not -nd <= axis < nd:
+                raise ValueError(f"{_LABEL} {op}: axis {axis} out of range for ndim {nd}")
+            return self._wrap(f(be, x, axis % nd, keepDims))
+        flat = be.reshape(x, (x.size,))
+        try:
+            r = f(be, flat, 0, False)
+        finally:
+            be.dispose(flat)
+        if keepDims:
+            kept = be.reshape(r, (1,) * nd)
+            be.dispose(r)
+            r = kept
+        return self._wrap(r)
+
+    # element-wise arithmetic (NumPy broadcasting, matching dtypes)
+    def add(self, other) -> "DeviceArray":
+        return self._binary("add", other, "numeric", lambda b, x, y: b.add(x, y))
+
+    def sub(self, other) -> "DeviceArray":
+        return self._binary("sub", other, "numeric", lambda b, x, y: b.sub(x, y))
+
+    def mul(self, other) -> "DeviceArray":
+        return self._binary("mul", other, "numeric", lambda b, x, y: b.mul(x, y))
+
+    def div(self, other) -> "DeviceArray":
+        return self._binary("div", other, "numeric", lambda b, x, y: b.div(x, y))
+
+    def maximum(self, other) -> "DeviceArray":
+        return self._binary("maximum", other, "numeric", lambda b, x, y: b.maximum(x, y))
+
+    def minimum(self, other) -> "DeviceArray":
+        """Composed as -maximum(-a, -b), as the reference does (device-array.ts:304-307)."""
+        def f(b, x, y):
+            nx, ny = b.neg(x), b.neg(y)
+            m = b.maximum(nx, ny)
+            r = b.neg(m)
+            for t in (nx, ny, m):
+                b.dispose(t)
+            return r
+        return self._binary("minimum", other, "numeric", f)
+
+    def pow(self, other) -> "DeviceArray":
+        return self._binary("pow", other, "float", lambda b, x, y: b.pow(x, y))
+
+    # unary math
+    def neg(self):
+        return self._unary("neg", "numeric", lambda b, x: b.neg(x))
+
+    def abs(self):
+        return self._unary("abs", "numeric", lambda b, x: b.abs(x))
+
+    def exp(self):
+        return self._unary("exp", "float", lambda b, x: b.exp(x))
+
+    def log(self):
+        return self._unary("log", "float", lambda b, x: b.log(x))
+
+    def sqrt(self):
+        return self._unary("sqrt", "float", lambda b, x: b.sqrt(x))
+
+    def rsqrt(self):
+        return self._unary("rsqrt", "float", lambda b, x: b.rsqrt(x))
+
+    def tanh(self):
+        return self._unary("tanh", "float", lambda b, x: b.tanh(x))
+
+    def sigmoid(self):
+        return self._unary("sigmoid", "float", lambda b, x: b.sigmoid(x))
+
+    def erf(self):
+        return self._unary("erf", "float", lambda b, x: b.erf(x))
+
+    def relu(self):
+        return self._unary("relu", "numeric", lambda b, x: b.relu(x))
+
+    # comparisons & logic (bool results)
+    def equal(self, other):
+        return self._binary("equal", other, "any", lambda b, x, y: b.equal(x, y))
+
+    def notEqual(self, other):
+        return self._binary("notEqual", other, "any", lambda b, x, y: b.notEqual(x, y))
+
+    def less(self, other):
+        return self._binary("less", other, "any", lambda b, x, y: b.less(x, y))
+
+    def lessEqual(self, other):
+        return self._binary("lessEqual", other, "any", lambda b, x, y: b.lessEqual(x, y))
+
+    def greater(self, other):
+        return self._binary("greater", other, "any", lambda b, x, y: b.greater(x, y))
+
+    def greaterEqual(self, other):
+        return self._binary("greaterEqual", other, "any", lambda b, x, y: b.greaterEqual(x, y))
+
+    def logicalAnd(self, other):
+        return self._binary("logicalAnd", other, "bool", lambda b, x, y: b.logicalAnd(x, y))
+
+    def logicalOr(self, other):
+        return self._binary("logicalOr", other, "bool", lambda b, x, y: b.logicalOr(x, y))
+
+    def logicalNot(self):
+        return self._unary("logicalNot", "bool", lambda b, x: b.logicalNot(x))
+
+    # reductions & scans
+    def sum(self, axis=None, keepDims: bool = False):
+        return self._reduce("sum", "numeric", axis, keepDims, lambda b, x, a, k: b.sum(x, a, k))
+
+    def mean(self, axis=None, keepDims: bool = False):
+        return self._reduce("mean", "float", axis, keepDims, lambda b, x, a, k: b.mean(x, a, k))
+
+    def max(self, axis=None, keepDims: bool = False):
+        return self._reduce("max", "numeric", axis, keepDims, lambda b, x, a, k: b.max(x, a, k))
+
+    def min(self, axis=None, keepDims: bool = False):
+        return self._reduce("min", "numeric", axis, keepDims, lambda b, x, a, k: b.min(x, a, k))
+
+    def argmax(self, axis=None, keepDims: bool = False):
+        return self._reduce("argmax", "numeric", axis, keepDims, lambda b, x, a, k: b.argmax(x, a, k))
+
+    def argmin(self, axis=None, keepDims: bool = False):
+        return self._reduce("argmin", "numeric", axis, keepDims, lambda b, x, a, k: b.argmin(x, a, k))
+
+    def cumsum(self, axis=None):
+        """Inclusive prefix sum along ``axis``; with no axis, over the flattened array."""
+        x = self._check("cumsum", "numeric")
+        be = self.device.backend
+        if axis is not None:
+            return self._wrap(be.cumsum(x, axis))
+        flat = be.reshape(x, (x.size,))
+        try:
+            return self._wrap(be.cumsum(flat, 0))
+        finally:
+            be.dispose(flat)
 
     def gelu(self) -> "DeviceArray":
         return self._wrap(self.device.backend.gelu(self._float("gelu")))

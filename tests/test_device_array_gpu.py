@@ -207,3 +207,28 @@ def test_residual_add_folds_into_the_gemm(dev):
         y.eval()
         assert dev.device.launch_count() - before == 1
         close(run(y.toTensor()).astype(np.float64), want, "bf16")
+
+
+def test_elementwise_reduction_and_scalar_operands(dev):
+    """device-array-suite.ts-style cases of the wider op set: number operands become constants of
+    the array's dtype, minimum is -maximum(-a, -b), reductions with no axis cover every element,
+    the dtype rules raise before any launch."""
+    x = np.array([[1.5, -2.0, 3.0], [0.5, 4.0, -1.0]], np.float32)
+    a = dev.from_numpy(x)
+    assert np.array_equal(run(a.mul(2).sub(1).toTensor()), x * 2 - 1)
+    assert np.array_equal(run(a.minimum(dev.from_numpy(np.zeros(3, np.float32))).toTensor()), np.minimum(x, 0))
+    assert run(a.sum().toTensor()).item() == np.float32(x.astype(np.float64).sum())
+    assert run(a.max(keepDims=True).toTensor()).shape == (1, 1)
+    assert run(a.argmax(1).toTensor()).tolist() == [2, 1]
+    assert run(a.cumsum().toTensor()).tolist() == np.cumsum(x.reshape(-1).astype(np.float64)).astype(np.float32).tolist()
+    gt = a.greater(0)
+    assert run(gt.toTensor()).tolist() == (x > 0).tolist()
+    w = dev.where(gt, a, a.neg())
+    assert np.array_equal(run(w.toTensor()), np.abs(x))
+    assert run(gt.logicalNot().logicalAnd(gt).toTensor()).tolist() == [[False] * 3] * 2
+    with pytest.raises(TypeError, match="needs a float dtype"):
+        dev.from_numpy(np.ones((2,), np.int32)).exp()
+    with pytest.raises(TypeError, match="cast\\(\"bool\"\\) first"):
+        a.logicalNot()
+    with pytest.raises(TypeError, match="not defined for bool"):
+        gt.sum()
