@@ -82,12 +82,23 @@ class GPT2:
     """The model's weights resident on one device and its forward pass."""
 
     def __init__(self, backend: CudaBackend, cfg: GPT2Config, weights: dict):
+        """``weights``: host arrays (uint16 = bf16 bits, else f32), uploaded here, or device
+        tensors (``CudaTensor``, e.g. from ``safetensors.gpt2_device_weights``), taken as they are."""
         self.backend, self.cfg = backend, cfg
         self.w: dict[str, CudaTensor] = {}
         for name, arr in weights.items():
+            if isinstance(arr, CudaTensor):
+                self.w[name] = arr
+                continue
             dtype = "bf16" if arr.dtype == np.uint16 else "f32"
             self.w[name] = backend.from_host_sync(host(dtype, arr.shape, arr))
         self._pos: dict[int, CudaTensor] = {}
+
+    @classmethod
+    def from_safetensors(cls, backend: CudaBackend, cfg: GPT2Config, source) -> "GPT2":
+        """A Hugging Face GPT-2 checkpoint (a ``.safetensors`` path or its bytes) on the device."""
+        from .safetensors import gpt2_device_weights
+        return cls(backend, cfg, gpt2_device_weights(source, backend, cfg.n_layer))
 
     def _positions(self, seq: int) -> CudaTensor:
         if seq not in self._pos:
