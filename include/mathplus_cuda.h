@@ -250,6 +250,28 @@ int mpc_cumsum(mpc_device *dev, const void *x, int32_t dtype_in, void *out, int3
 /* out[Σ i_k·out_strides_k] = x[Σ i_k·x_strides_k] over shape[rank]: slice, concat, broadcast copies. */
 int mpc_strided_copy(mpc_device *dev, const void *x, const int64_t *x_strides, void *out, const int64_t *out_strides,
                      int32_t elem_bytes, int32_t rank, const int64_t *shape, mpc_stream s);
+/* Ascending sort of every lane along the middle axis of a contiguous [outer, dim, inner]
+ * (Backend.sort -> sortAxis, tensor-cpu/src/index.ts:724-734, kernels.ts:601-617): numeric order,
+ * -0 before +0, NaN last; any dtype. */
+int mpc_sort(mpc_device *dev, const void *x, int32_t dtype, void *out, int64_t outer, int64_t dim, int64_t inner,
+             mpc_stream s);
+/* Per-batch row gather (Backend.gatherRows, tensor-cpu/src/index.ts:793-810): x [B, L, D], idx i32
+ * [B, M] (a negative index counts from the end) -> out [B, M, D] in x's dtype. An index outside
+ * [-L, L) fails with MPC_ERR_INVALID and its flat position in *bad_index (synchronises). */
+int mpc_gather_rows(mpc_device *dev, const void *x, int32_t dtype, const int32_t *idx, void *out, int64_t B, int64_t L,
+                    int64_t M, int64_t D, int64_t *bad_index, mpc_stream s);
+/* Split-half rotary embedding over bh contiguous [L, dh] blocks, positions 0..L-1 (Backend.rope ->
+ * ropeHalf, tensor-cpu/src/index.ts:812-819, nn-kernels.ts:138-160); dh even. */
+int mpc_rope(mpc_device *dev, const void *x, int32_t dtype, void *out, int64_t bh, int64_t L, int64_t dh, double base,
+             mpc_stream s);
+/* GEGLU over rows of 2d: out[r, j] = GELU(x[r, j]) * x[r, d + j] (Backend.geglu -> gegluRows,
+ * tensor-cpu/src/index.ts:842-850, nn-kernels.ts:245-250). */
+int mpc_geglu(mpc_device *dev, const void *x, int32_t dtype, void *out, int64_t rows, int64_t d, mpc_stream s);
+/* Masked mean over axis 1: x [B, L, D], mask [B, L] (nonzero = keep; any dtype) -> out [B, D]; a
+ * row with nothing kept gives 0 (Backend.meanPool -> maskedMeanPool, tensor-cpu/src/index.ts:852-860,
+ * nn-kernels.ts:256-271). */
+int mpc_mean_pool(mpc_device *dev, const void *x, int32_t dtype, const void *mask, int32_t mask_dtype, void *out,
+                  int64_t B, int64_t L, int64_t D, mpc_stream s);
 
 /* ---- multi-GPU: NCCL over NVLink, one rank per process (no reference counterpart) ---------- */
 int mpc_comm_unique_id(void *id128);

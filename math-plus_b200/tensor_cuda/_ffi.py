@@ -111,6 +111,11 @@ SIGNATURES = {
     "mpc_reduce": [_dev, _i32, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _vp],
     "mpc_cumsum": [_dev, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _vp],
     "mpc_strided_copy": [_dev, _vp, C.POINTER(_i64), _vp, C.POINTER(_i64), _i32, _i32, C.POINTER(_i64), _vp],
+    "mpc_sort": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, _vp],
+    "mpc_gather_rows": [_dev, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, C.POINTER(_i64), _vp],
+    "mpc_rope": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, C.c_double, _vp],
+    "mpc_geglu": [_dev, _vp, _i32, _vp, _i64, _i64, _vp],
+    "mpc_mean_pool": [_dev, _vp, _i32, _vp, _i32, _vp, _i64, _i64, _i64, _vp],
     "mpc_gemm_residual": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp, _vp],
     "mpc_gemm_f32_noalloc": [C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
     "mpc_sdpa": [_dev, C.POINTER(SdpaDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp],

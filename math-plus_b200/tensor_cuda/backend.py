@@ -779,3 +779,81 @@ class CudaBackend:
             raise IndexError(f"tensor-cuda: embedding: id at position {bad.value} out of range [0, {V})")
         F.check(rc, "mpc_embedding")
         return out
+
+    # ---- sort, row gather, rotary embedding, GEGLU, masked mean pool ----------------------------
+    # (CpuBackendImpl, packages/tensor-cpu/src/index.ts:724-861): f64 arithmetic with one rounding;
+    # results keep the input's dtype where the CPU backend returns f32 (f32 inputs give its bits).
+    def sort(self, x: CudaTensor, axis: int = -1) -> CudaTensor:
+        """Ascending along ``axis``: numeric order, -0 before +0, NaN last (sortAxis)."""
+        self._check_live(x)
+        _, outer, dim, inner = self._around(x.shape, axis)
+        out = self._alloc(x.shape, x.dtype)
+        F.call("mpc_sort", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(out._buf.ptr),
+               outer, dim, inner, None)
+        return out
+
+    def gatherRows(self, x: CudaTensor, idx: CudaTensor) -> CudaTensor:
+        """x [B, L, D], idx i32 [B, M] -> [B, M, D]: out[b, m] = x[b, idx[b, m]], a negative index
+        counting from the end (index.ts:793-810)."""
+        self._check_live(x, idx)
+        if len(x.shape) != 3 or len(idx.shape) != 2 or idx.shape[0] != x.shape[0]:
+            raise ValueError(f"tensor-cuda: gatherRows [{','.join(map(str, x.shape))}] idx "
+                             f"[{','.join(map(str, idx.shape))}]")
+        if idx.dtype != "i32":
+            raise TypeError("tensor-cuda: gatherRows idx is i32")
+        B, L, D = x.shape
+        M = idx.shape[1]
+        out = self._alloc((B, M, D), x.dtype)
+        bad = C.c_int64(-1)
+        rc = F.load().mpc_gather_rows(self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype],
+                                      C.c_void_p(idx.ptr), C.c_void_p(out._buf.ptr), B, L, M, D, C.byref(bad), None)
+        if rc == F.ERR_INVALID and bad.value >= 0:
+            raw = self.read_sync(self.slice(self.reshape(idx, (B * M,)), [bad.value], [bad.value + 1])).data[0]
+            out._release()
+            raise IndexError(f"tensor-cuda: gatherRows index {int(raw)} out of range for length {L}")
+        F.check(rc, "mpc_gather_rows")
+        return out
+
+    def rope(self, x: CudaTensor, base: float = 10000.0) -> CudaTensor:
+        """Split-half rotary embedding of x [B, H, L, Dh], positions 0..L-1 (ropeHalf)."""
+        self._check_live(x)
+        if len(x.shape) != 4:
+            raise ValueError(f"tensor-cuda: rope expects [B, H, L, Dh], got [{','.join(map(str, x.shape))}]")
+        B, H, L, Dh = x.shape
+        if Dh % 2:
+            raise ValueError(f"tensor-cuda: rope needs an even head dim, got {Dh}")
+        if x.dtype not in FLOAT:
+            raise TypeError(f"tensor-cuda: rope: float dtypes only, got {x.dtype}")
+        out = self._alloc(x.shape, x.dtype)
+        F.call("mpc_rope", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(out._buf.ptr),
+               B * H, L, Dh, C.c_double(base), None)
+        return out
+
+    def geglu(self, x: CudaTensor) -> CudaTensor:
+        """[..., 2D] -> [..., D]: GELU(first half) * second half (gegluRows)."""
+        self._check_live(x)
+        d2 = x.shape[-1] if x.shape else 0
+        if not x.shape or d2 % 2:
+            raise ValueError(f"tensor-cuda: geglu needs an even last axis, got {d2}")
+        if x.dtype not in FLOAT:
+            raise TypeError(f"tensor-cuda: geglu: float dtypes only, got {x.dtype}")
+        D = d2 // 2
+        rows = x.size // d2 if d2 else 0
+        out = self._alloc(tuple(x.shape[:-1]) + (D,), x.dtype)
+        F.call("mpc_geglu", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(out._buf.ptr),
+               rows, D, None)
+        return out
+
+    def meanPool(self, x: CudaTensor, mask: CudaTensor) -> CudaTensor:
+        """x [B, L, D], mask [B, L] (nonzero = keep) -> [B, D] (maskedMeanPool)."""
+        self._check_live(x, mask)
+        if len(x.shape) != 3 or len(mask.shape) != 2 or tuple(mask.shape) != tuple(x.shape[:2]):
+            raise ValueError(f"tensor-cuda: meanPool x [{','.join(map(str, x.shape))}] mask "
+                             f"[{','.join(map(str, mask.shape))}]")
+        if x.dtype not in FLOAT:
+            raise TypeError(f"tensor-cuda: meanPool: float dtypes only, got {x.dtype}")
+        B, L, D = x.shape
+        out = self._alloc((B, D), x.dtype)
+        F.call("mpc_mean_pool", self.device.handle, C.c_void_p(x.ptr), F.DTYPE_CODES[x.dtype], C.c_void_p(mask.ptr),
+               F.DTYPE_CODES[mask.dtype], C.c_void_p(out._buf.ptr), B, L, D, None)
+        return out

@@ -599,3 +599,62 @@ long mp_take_rows_f32(const float *table, int row_len, int n_rows, const int32_t
   }
   return -1;
 }
+
+/* nn-kernels.ts:138-160 (ropeHalf): split-half rotary embedding over BH contiguous [L, Dh]
+ * blocks. inv_freq = f32(2^f32(-f32(i/half) * f32(log2 base))), theta = f32(p * inv_freq), cos and
+ * sin in f64, the rotation in f64 (no contraction: -ffp-contract=off), one f32 rounding. */
+void mp_rope_half_f32(const float *x, int BH, int L, int Dh, double base, float *o) {
+  const int half = Dh / 2;
+  const float lb = (float)log2(base);
+  double *cs = malloc(sizeof(double) * (size_t)L * half * 2);
+  for (int i = 0; i < half; i++) {
+    const float fi = (float)((double)i / half);
+    const float invf = (float)pow(2.0, (double)(float)(-(double)fi * lb));
+    for (int p = 0; p < L; p++) {
+      const float th = (float)((double)p * invf);
+      cs[((size_t)p * half + i) * 2] = cos(th);
+      cs[((size_t)p * half + i) * 2 + 1] = sin(th);
+    }
+  }
+  for (int bh = 0; bh < BH; bh++) {
+    for (int p = 0; p < L; p++) {
+      const float *s = x + ((size_t)bh * L + p) * Dh;
+      float *d = o + ((size_t)bh * L + p) * Dh;
+      for (int i = 0; i < half; i++) {
+        const double x1 = s[i], x2 = s[half + i];
+        const double c = cs[((size_t)p * half + i) * 2], sn = cs[((size_t)p * half + i) * 2 + 1];
+        d[i] = (float)(x1 * c - x2 * sn);
+        d[half + i] = (float)(x2 * c + x1 * sn);
+      }
+    }
+  }
+  free(cs);
+}
+
+/* nn-kernels.ts:245-250 (gegluRows): o[r, j] = geluErf(x[r, j]) * x[r, D + j]. */
+void mp_geglu_rows_f32(const float *x, int rows, int D, float *o) {
+  for (int r = 0; r < rows; r++) {
+    const float *s = x + (size_t)r * 2 * D;
+    for (int j = 0; j < D; j++) o[(size_t)r * D + j] = (float)(mp_gelu_erf(s[j]) * s[D + j]);
+  }
+}
+
+/* nn-kernels.ts:256-271 (maskedMeanPool): f64 sums over kept positions (mask nonzero, NaN falsy),
+ * times 1 / max(count, 1). */
+void mp_masked_mean_pool_f32(const float *x, int B, int L, int D, const float *mask, float *o) {
+  double *acc = malloc(sizeof(double) * (size_t)(D > 0 ? D : 1));
+  for (int b = 0; b < B; b++) {
+    for (int j = 0; j < D; j++) acc[j] = 0;
+    int cnt = 0;
+    for (int l = 0; l < L; l++) {
+      const float m = mask[(size_t)b * L + l];
+      if (m == 0 || m != m) continue;
+      cnt++;
+      const float *s = x + ((size_t)b * L + l) * D;
+      for (int j = 0; j < D; j++) acc[j] += s[j];
+    }
+    const double inv = 1.0 / (cnt > 1 ? cnt : 1);
+    for (int j = 0; j < D; j++) o[(size_t)b * D + j] = (float)(acc[j] * inv);
+  }
+  free(acc);
+}

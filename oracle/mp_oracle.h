@@ -89,6 +89,9 @@ void mp_gelu_f32(const float *x, size_t n, float *out);
 /* takeRows (nn-kernels.ts:277-286); returns the first bad index position or -1. */
 long mp_take_rows_f32(const float *table, int row_len, int n_rows, const int32_t *idx, size_t n_idx,
                       float *out);
+void mp_rope_half_f32(const float *x, int BH, int L, int Dh, double base, float *o);
+void mp_geglu_rows_f32(const float *x, int rows, int D, float *o);
+void mp_masked_mean_pool_f32(const float *x, int B, int L, int D, const float *mask, float *o);
 
 #ifdef __cplusplus
 }

@@ -68,6 +68,9 @@ def lib() -> C.CDLL:
         L.mp_gelu_f32.argtypes = [vp, sz, vp]
         L.mp_take_rows_f32.argtypes = [vp, C.c_int, C.c_int, vp, sz, vp]
         L.mp_take_rows_f32.restype = C.c_long
+        L.mp_rope_half_f32.argtypes = [vp, C.c_int, C.c_int, C.c_int, f64, vp]
+        L.mp_geglu_rows_f32.argtypes = [vp, C.c_int, C.c_int, vp]
+        L.mp_masked_mean_pool_f32.argtypes = [vp, C.c_int, C.c_int, C.c_int, vp, vp]
         _lib = L
     return _lib
 
@@ -287,6 +290,63 @@ def embedding(table, ids) -> np.ndarray:
     bad = lib().mp_take_rows_f32(_ptr(table), D, V, _ptr(ids), ids.size, _ptr(out))
     if bad >= 0:
         raise IndexError(f"takeRows: row index {int(ids.reshape(-1)[bad])} out of range [0, {V})")
+    return out
+
+
+def sort_axis(x, axis: int = -1) -> np.ndarray:
+    """``CpuBackendImpl.sort`` -> ``sortAxis`` (tensor-cpu/src/index.ts:724-734, kernels.ts:601-617):
+    each lane sorted by the typed-array order (numeric ascending, -0 before +0, NaN last)."""
+    x = np.asarray(x)
+    if x.dtype.kind == "f":
+        f = x.astype(np.float32)
+        bits = f.view(np.uint32)
+        key = np.where(bits & 0x80000000, ~bits, bits | 0x80000000).astype(np.uint32)
+        key = np.where(np.isnan(f), np.uint32(0xFFFFFFFF), key)
+        order = np.argsort(key, axis=axis, kind="stable")
+        return np.take_along_axis(x, order, axis=axis)
+    return np.sort(x, axis=axis, kind="stable")
+
+
+def gather_rows(x, idx) -> np.ndarray:
+    """``CpuBackendImpl.gatherRows`` (tensor-cpu/src/index.ts:793-810): x [B, L, D], idx [B, M]
+    (negative counts from the end) -> [B, M, D] via takeRows."""
+    x = np.asarray(x)
+    idx = np.asarray(idx, np.int64)
+    B, L, D = x.shape
+    r = np.where(idx < 0, idx + L, idx)
+    bad = np.argwhere((r < 0) | (r >= L))
+    if bad.size:
+        b, m = bad[0]
+        raise IndexError(f"gatherRows index {int(idx[b, m])} out of range for length {L}")
+    return x[np.arange(B)[:, None], r]
+
+
+def rope(x, base: float) -> np.ndarray:
+    """``CpuBackendImpl.rope`` -> ``ropeHalf`` (tensor-cpu/src/index.ts:812-819, nn-kernels.ts:138-160)."""
+    x = _f32(x)
+    B, H, L, Dh = x.shape
+    out = np.empty_like(x)
+    lib().mp_rope_half_f32(_ptr(x), B * H, L, Dh, float(base), _ptr(out))
+    return out
+
+
+def geglu(x) -> np.ndarray:
+    """``CpuBackendImpl.geglu`` -> ``gegluRows`` (tensor-cpu/src/index.ts:842-850, nn-kernels.ts:245-250)."""
+    x = _f32(x)
+    D = x.shape[-1] // 2
+    out = np.empty(x.shape[:-1] + (D,), np.float32)
+    lib().mp_geglu_rows_f32(_ptr(x), x.size // (2 * D) if D else 0, D, _ptr(out))
+    return out
+
+
+def mean_pool(x, mask) -> np.ndarray:
+    """``CpuBackendImpl.meanPool`` -> ``maskedMeanPool`` (tensor-cpu/src/index.ts:852-860,
+    nn-kernels.ts:256-271)."""
+    x = _f32(x)
+    B, L, D = x.shape
+    m = _f32(np.asarray(mask, np.float64))
+    out = np.empty((B, D), np.float32)
+    lib().mp_masked_mean_pool_f32(_ptr(x), B, L, D, _ptr(m), _ptr(out))
     return out
 
 

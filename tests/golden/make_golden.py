@@ -9,7 +9,8 @@ It drives, as subprocesses and through their documented stdin/job-file interface
 
 * packages/tensor-webgpu/scripts/gemm_oracle.py       (C = A@B and |A|@|B| in f64)
 * packages/tensor-webgpu/scripts/attention_oracle.py  (masked softmax attention in f64)
-* packages/tensor-cpu/scripts/numpy_oracle.py         (linear / matmul / sdpa / softmax / gelu)
+* packages/tensor-cpu/scripts/numpy_oracle.py         (linear / matmul / sdpa / softmax / gelu /
+                                                       rope / geglu / mean_pool / sort / gather_rows)
 * packages/special/scripts/special_oracle.py          (SciPy erf / erfc / x*ndtr(x))
 
 Inputs come from the reference tests' own generators, restated here in pure
@@ -202,7 +203,8 @@ def attention_fixtures(ref: str) -> dict:
 # ---- tensor-cpu differential cases: packages/tensor-cpu/test/differential.test.ts -------
 
 def differential_fixtures(ref: str) -> dict:
-    """linear / matmul / sdpa / softmax / gelu cases from differential.test.ts:96-120, through numpy_oracle.py."""
+    """linear / matmul / sdpa / softmax / gelu / rope / geglu / meanPool / sort / gatherRows cases from
+    differential.test.ts:96-160, through numpy_oracle.py."""
     script = os.path.join(ref, "packages/tensor-cpu/scripts/numpy_oracle.py")
     counter = [0]
 
@@ -267,6 +269,22 @@ def differential_fixtures(ref: str) -> dict:
     add("softmax_mid_axis", "softmax", {"axis": 1}, [x[3]], [x[:3]])
     x = f32((200,), -10, 10)
     add("gelu_200", "unary", {"fn": "gelu"}, [x[3]], [x[:3]])
+    # differential.test.ts:109-116, 153, 160: rope, geglu, meanPool, sort, gatherRows
+    x = f32((1, 3, 17, 16))
+    add("rope_base10000_1x3x17x16", "rope", {"base": 10000.0}, [x[3]], [x[:3]])
+    x = f32((2, 2, 70, 32))
+    add("rope_base160000_2x2x70x32", "rope", {"base": 160000.0}, [x[3]], [x[:3]])
+    x = f32((3, 5, 24), -6, 6)
+    add("geglu_3x5x24", "geglu", {}, [x[3]], [x[:3]])
+    x = f32((3, 7, 5))
+    pool_mask = np.array([1, 1, 0, 1, 0, 0, 1, 0, 0, 0, 0, 0, 0, 0, 1, 1, 1, 1, 1, 1, 1], np.bool_).reshape(3, 7)
+    add("mean_pool_3x7x5", "mean_pool", {}, [x[3], pool_mask], [x[:3]])
+    x = f32((5, 3))
+    add("sort_axis0_5x3", "sort", {"axis": 0}, [x[3]], [x[:3]])
+    x = f32((2, 7, 3))
+    counter[0] += 1
+    gather_idx = np.floor(lcg_seeded(8, 104729 * counter[0], -7, 7)).astype(np.int32).reshape(2, 4)
+    add("gather_rows_2x7x3_idx2x4", "gather_rows", {}, [x[3], gather_idx], [x[:3]])
 
     fx = {}
     with tempfile.TemporaryDirectory() as d:
@@ -291,6 +309,12 @@ def differential_fixtures(ref: str) -> dict:
             fx[name + "_ranks"] = np.array([t.ndim for t in tensors], np.int64)
             if op == "sdpa" and len(tensors) > 3:
                 fx[name + "_mask"] = tensors[3]
+            if op == "mean_pool":
+                fx[name + "_mask"] = tensors[1]
+            if op == "gather_rows":
+                fx[name + "_idx"] = tensors[1]
+            if "base" in args:
+                fx[name + "_base"] = np.array([args["base"]], np.float64)
             if "scale" in args:
                 fx[name + "_scale"] = np.array([args["scale"]], np.float64)
             if "axis" in args:
@@ -324,11 +348,16 @@ def special_fixtures(ref: str) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ref = ap.parse_args().reference
-    np.savez_compressed(os.path.join(HERE, "gemm_webgpu.npz"), **gemm_fixtures(ref))
-    np.savez_compressed(os.path.join(HERE, "attention_webgpu.npz"), **attention_fixtures(ref))
-    np.savez_compressed(os.path.join(HERE, "differential_cpu.npz"), **differential_fixtures(ref))
-    np.savez_compressed(os.path.join(HERE, "special.npz"), **special_fixtures(ref))
+    ap.add_argument("--only", choices=["gemm", "attention", "differential", "special"],
+                    help="regenerate one fixture file")
+    args = ap.parse_args()
+    ref = args.reference
+    makers = {"gemm": ("gemm_webgpu.npz", gemm_fixtures), "attention": ("attention_webgpu.npz", attention_fixtures),
+              "differential": ("differential_cpu.npz", differential_fixtures),
+              "special": ("special.npz", special_fixtures)}
+    for key, (fname, make) in makers.items():
+        if args.only in (None, key):
+            np.savez_compressed(os.path.join(HERE, fname), **make(ref))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))
