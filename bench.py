@@ -21,6 +21,11 @@ A step is one pass of the hot path over one batch of synthetic input:
                                shard-major copy of C over NVLink (the all-gather fused into the
                                GEMM), then a local permute to row-major. The line also carries the
                                blocked-view-only, GEMM-only and GEMM + NCCL all-gather + permute times.
+  fused_elementwise_f32        the tensor-compile chain (x + y) * z -> sigmoid -> relu over three f32
+                               inputs of 2^28 elements, fused into one kernel (WebGpuDevice.fuse,
+                               packages/tensor-webgpu/src/facade.ts:137-164; the chain of
+                               packages/tensor-webgpu/test/fusion.test.ts:157-163); GB/s of the
+                               16 bytes each element reads and writes.
 
 ``value`` is device-timed throughput with inputs resident in HBM (CUDA events on the launching
 stream, barrier + synchronize around the timed region, max over ranks). ``e2e`` runs the same
@@ -60,6 +65,10 @@ WORKLOADS = {
                               metric="GPT-2-small forward TFLOP/s (bf16)",
                               desc="GPT-2-small-shaped forward (12 layers, d 768, 12 heads, d_ff 3072, vocab 50257), "
                                    "batch 32 x 1024 tokens, random-init bf16 weights ~ N(0, 0.02), logits bf16"),
+    "fused_elementwise_f32": dict(kind="fusion", n=1 << 28, dtype="f32", unit="GB/s",
+                                  metric="fused element-wise GB/s ((x + y) * z -> sigmoid -> relu, f32)",
+                                  desc="one fused kernel over three f32 inputs of 2^28 elements: "
+                                       "relu(sigmoid((x + y) * z)), f64 evaluation, f32 out (16 bytes per element)"),
     "causal_attention_f16": dict(kind="attention", batch=16, heads=32, seq=2048, head_dim=128, dtype="f16",
                                  causal=True, metric="fused attention TFLOP/s (causal f16)",
                                  desc="causal sdpa f16 [16,32,2048,128], scale 1/sqrt(128), f16 out + f32 LSE"),
@@ -77,6 +86,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work for the baseline sample")
     ap.add_argument("--batch", type=int, default=None, help="override the per-rank batch (small profiling cases)")
+    ap.add_argument("--elements", type=int, default=None,
+                    help="override the element count of the fused element-wise workload (small profiling cases)")
     return ap.parse_args()
 
 
@@ -167,7 +178,21 @@ def dist_env():
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
+def unit_of(w):
+    """(unit, scale): throughput is work per second / scale."""
+    return (w["unit"], 1e9) if w.get("unit") == "GB/s" else ("TFLOP/s", 1e12)
+
+
+def fusion_expr():
+    sys.path.insert(0, os.path.join(ROOT, "math-plus_b200"))
+    from tensor_cuda.fusion import Traced
+    return Traced.input(0).add(Traced.input(1)).mul(Traced.input(2)).sigmoid().relu()
+
+
 def flop_per_step(w):
+    """Work per step: FLOP, or bytes for the HBM-bound fused element-wise workload."""
+    if w["kind"] == "fusion":
+        return 16.0 * w["n"]
     if w["kind"] == "gpt2":
         sys.path.insert(0, os.path.join(ROOT, "math-plus_b200"))
         from tensor_cuda.gpt2 import GPT2Config
@@ -188,6 +213,19 @@ def cpu_sample_rate(w: dict, target_s: float, threads: int):
     import numpy as np
     import oracle as O
     rng = np.random.default_rng(7)
+    if w["kind"] == "fusion":
+        node = fusion_expr().node
+        n = 1 << 16
+        while True:
+            xs = [rng.standard_normal(n).astype(np.float32) for _ in range(3)]
+            t0 = time.perf_counter()
+            O.eval_ir(node, xs)
+            dt = time.perf_counter() - t0
+            if dt >= target_s / 4 or n >= w["n"]:
+                break
+            n = min(w["n"], n * 4)
+        return 16.0 * n / dt, (f"{n} of the {w['n']} elements through the oracle's restatement of "
+                               "tensor-compile's evaluator (evalValue, f64, one thread)"), dt
     if w["kind"] == "gpt2":
         sys.path.insert(0, os.path.join(ROOT, "math-plus_b200"))
         from tensor_cuda.gpt2 import GPT2Config, random_weights
@@ -263,22 +301,24 @@ def run_reference(args, w):
         return
     threads = len(os.sched_getaffinity(0))
     rates, sample = [], ""
+    unit, scale = unit_of(w)
     per = max(1.0, min(args.cpu_seconds, 150.0 / max(1, args.warmup + args.steps)))
     for i in range(args.warmup + args.steps):
         r, sample, _ = cpu_sample_rate(w, per, threads)
         if i >= args.warmup:
             rates.append(r)
-    v = statistics.median(rates) / 1e12
+    v = statistics.median(rates) / scale
     line = {
-        "impl": "reference", "metric": w["metric"], "value": v, "unit": "TFLOP/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": flop_per_step(w) / (v * 1e12) * 1e3,
+        "impl": "reference", "metric": w["metric"], "value": v, "unit": unit, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": flop_per_step(w) / (v * scale) * 1e3,
         "higher_is_better": True, "scaling": "strong" if w["kind"] == "nsplit" else "weak", "vs_baseline": None,
         "dtype": "f64 (f32 storage)",
         "data": "synthetic", "config": {"workload": args.workload, "description": w["desc"]},
-        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": "per step: " + sample + "; the oracle's restatement of tensor-core "
-                                   "gemmNT / attention, OpenMP over row blocks / heads"},
-        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": v, "unit": unit, "cores": 1 if w["kind"] == "fusion" else threads, "kind": "port",
+                         "sample": "per step: " + sample + ("" if w["kind"] == "fusion" else
+                                   "; the oracle's restatement of tensor-core gemmNT / attention, OpenMP over "
+                                   "row blocks / heads")},
+        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     emit(line)
 
@@ -350,6 +390,19 @@ def setup_nsplit(w, dev, torch, g, local, F, world, pg):
     extras = {"group": group, "fused": fused, "pl": pl,
               "gemm_desc": gemm_desc(M, n, K, F.BF16, F.DTYPE_CODES[w["out"]], F.B_KN)}
     return [A, Bs], Out, launch, "gemm_kernel<kHalf, B MN-major, BN=256, 4 stages, 8 output maps>", extras
+
+
+def setup_fusion(w, dev, torch, g, local, F):
+    from tensor_cuda.fusion import kernel_for
+    n = w["n"]
+    ins = [torch.randn((n,), generator=g, device=f"cuda:{local}") for _ in range(3)]
+    out = dev.alloc(4 * n)
+    k = kernel_for(dev, fusion_expr().node, ["f32"] * 3)
+
+    def launch(ptrs, optr, stream):
+        k.run(ptrs, [(n,)] * 3, (n,), optr, stream)
+
+    return ins, out, launch, "mpc_fused_flat (NVRTC-compiled for sm_100a: 16-byte loads, f64 evaluation)"
 
 
 def setup_gpt2(w, dev, torch, g, local, F, rank):
@@ -426,6 +479,8 @@ def run_ours(args, w):
         ins, out, launch, kernel_name, extras = setup_nsplit(w, dev, torch, g, local, F, world, pg)
     elif w["kind"] == "gpt2":
         ins, out, launch, kernel_name = setup_gpt2(w, dev, torch, g, local, F, rank)
+    elif w["kind"] == "fusion":
+        ins, out, launch, kernel_name = setup_fusion(w, dev, torch, g, local, F)
     else:
         setup = setup_gemm if w["kind"] == "gemm" else setup_attention
         ins, out, launch, kernel_name = setup(w, dev, torch, g, local, F)
@@ -487,8 +542,9 @@ def run_ours(args, w):
 
     ms_total = max_over_ranks(ms_total)
     ms_step = ms_total / args.steps
+    unit, scale = unit_of(w)
     job_flop = flop_step if strong else flop_step * world
-    value = job_flop / (ms_step * 1e-3) / 1e12
+    value = job_flop / (ms_step * 1e-3) / scale
 
     breakdown = None
     if strong:  # the same step as GEMM alone and as GEMM + NCCL all-gather + permute
@@ -543,7 +599,7 @@ def run_ours(args, w):
         dev.stream_sync(stream)
         barrier()
         ms_e2e = max_over_ranks(dev.elapsed_ms(x0, x1))
-        e2e = {"value": job_flop / (ms_e2e / args.e2e_steps * 1e-3) / 1e12, "unit": "TFLOP/s",
+        e2e = {"value": job_flop / (ms_e2e / args.e2e_steps * 1e-3) / scale, "unit": unit,
                "h2d_bytes_per_step": int(sum(h.nbytes for h, _, _ in hins)), "d2h_bytes_per_step": int(hout.nbytes),
                "ms_per_step": ms_e2e / args.e2e_steps,
                "path": "mpc_memcpy_h2d_async per input -> one kernel -> mpc_memcpy_d2h_async, pinned host buffers"}
@@ -556,11 +612,18 @@ def run_ours(args, w):
         long_region = ms_total > 2000
         peak = peaks["bf16_tflops_sustained"] if long_region else peaks["bf16_tflops"]
         rank_flop = flop_step / world if strong else flop_step
-        achieved = rank_flop / (ms_step * 1e-3) / 1e12  # one launch of the kernel per step and rank
-        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                "peak_source": f"{peaks['source']} bf16 dense ({'sustained' if long_region else 'burst'})",
-                "traffic": profiled_traffic(args.workload), "algorithmic_flop_per_launch": rank_flop,
-                "kernel": kernel_name}
+        achieved = rank_flop / (ms_step * 1e-3) / scale  # one launch of the kernel per step and rank
+        if w["kind"] == "fusion":
+            roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} HBM copy",
+                    "traffic": profiled_traffic(args.workload), "algorithmic_bytes_per_launch": rank_flop,
+                    "kernel": kernel_name}
+        else:
+            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak,
+                    "peak_source": f"{peaks['source']} bf16 dense ({'sustained' if long_region else 'burst'})",
+                    "traffic": profiled_traffic(args.workload), "algorithmic_flop_per_launch": rank_flop,
+                    "kernel": kernel_name}
         if strong and world > 1:
             # fused GEMM + all-gather: the slower of the tensor-core time and the NVLink time of the
             # bytes every GPU must receive ((p-1)/p of C), at the measured 770 GB/s per direction
@@ -579,10 +642,11 @@ def run_ours(args, w):
             try:
                 threads = len(os.sched_getaffinity(0))
                 r, sample, secs = cpu_sample_rate(w, args.cpu_seconds, threads)
-                cpu = {"value": r / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                cpu = {"value": r / scale, "unit": unit, "cores": 1 if w["kind"] == "fusion" else threads,
+                       "kind": "port",
                        "sample": sample + f" ({secs:.1f} s); the oracle's restatement of the reference's CPU path"}
             except Exception as ex:  # reported, never required
-                cpu = {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "port", "sample": f"failed: {ex}"}
+                cpu = {"value": None, "unit": unit, "cores": None, "kind": "port", "sample": f"failed: {ex}"}
         par = (f"column split over {world} GPUs, all-gather fused into the GEMM epilogue (peer stores into the "
                "shard-major view), then a local permute to row-major" if strong
                else f"dp{world} (shards, no collective)")
@@ -590,9 +654,11 @@ def run_ours(args, w):
         if breakdown:
             cfg["breakdown_ms_per_step"] = breakdown
         cfg.update({k: w[k] for k in ("batch", "m", "n", "k", "heads", "seq", "head_dim", "out") if k in w})
+        if w["kind"] == "fusion":
+            cfg["expression"] = "relu(sigmoid((x + y) * z))"
         cfg["l2"] = "flushed between steps (256 MiB write)" if flush is not None else "inputs larger than L2 (126 MB)"
         line = {
-            "metric": w["metric"], "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "metric": w["metric"], "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if strong else "weak",
             "vs_baseline": None, "dtype": w["dtype"],
@@ -628,6 +694,8 @@ def main():
     w = dict(WORKLOADS[args.workload])
     if args.batch is not None:
         w["batch"] = args.batch
+    if args.elements is not None and w["kind"] == "fusion":
+        w["n"] = args.elements
     if args.impl == "reference":
         run_reference(args, w)
     else:

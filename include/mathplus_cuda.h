@@ -43,7 +43,8 @@ typedef enum {
   MPC_ERR_TIMEOUT = 5,     /* a kernel's bounded wait ran out; the kernel returned early */
   MPC_ERR_POISONED = 6,    /* an earlier fault poisoned this device handle: destroy it */
   MPC_ERR_NO_DEVICE = 7,   /* no CUDA device / not an sm_100 device */
-  MPC_ERR_COMM = 8         /* NCCL unavailable or a collective failed */
+  MPC_ERR_COMM = 8,        /* NCCL unavailable or a collective failed */
+  MPC_ERR_COMPILE = 9      /* NVRTC unavailable or it could not compile a fused expression */
 } mpc_status;
 
 typedef enum { MPC_F32 = 0, MPC_F16 = 1, MPC_BF16 = 2, MPC_I32 = 3, MPC_BOOL = 4 } mpc_dtype;
@@ -52,6 +53,7 @@ typedef struct mpc_device mpc_device; /* one per CUDA device ordinal and process
 typedef void *mpc_stream;             /* a cudaStream_t; NULL = the device's own stream */
 typedef void *mpc_event;              /* a cudaEvent_t */
 typedef struct mpc_comm mpc_comm;     /* an NCCL communicator (one rank of a group) */
+typedef struct mpc_fused mpc_fused;   /* a compiled fused element-wise expression */
 
 typedef struct {
   char name[128];
@@ -272,6 +274,42 @@ int mpc_geglu(mpc_device *dev, const void *x, int32_t dtype, void *out, int64_t 
  * nn-kernels.ts:256-271). */
 int mpc_mean_pool(mpc_device *dev, const void *x, int32_t dtype, const void *mask, int32_t mask_dtype, void *out,
                   int64_t B, int64_t L, int64_t D, mpc_stream s);
+
+/* ---- element-wise fusion (WebGpuDevice.fuse / compile, packages/tensor-webgpu/src/facade.ts:137-164,
+ * lowering as fusion-wgsl.ts:303-431) ------------------------------------------------------------
+ * A traced expression of the tensor-compile IR (packages/tensor-compile/src/ir.ts:66-72) as a DAG
+ * of instructions {op, a, b, c}, int32 each: MPC_IR_INPUT (a = input index), MPC_IR_CONST (a =
+ * index into consts), a unary op (a = operand), a binary or comparison op (a, b), MPC_IR_SELECT
+ * (a = condition, b = then, c = else); operands are indices of EARLIER instructions and the last
+ * instruction is the result. Every node evaluates in f64 with the reference's formulas and the
+ * result is rounded once to f32. The expression is compiled at run time (NVRTC, sm_100a) into one
+ * kernel. */
+enum {
+  MPC_IR_INPUT = 1, MPC_IR_CONST = 2, MPC_IR_SELECT = 3,
+  MPC_IR_NEG = 16, MPC_IR_RELU, MPC_IR_SIGMOID, MPC_IR_GELU, MPC_IR_GELU_TANH, MPC_IR_EXP, MPC_IR_LOG, MPC_IR_SQRT,
+  MPC_IR_SIN, MPC_IR_COS, MPC_IR_TAN, MPC_IR_ASIN, MPC_IR_ACOS, MPC_IR_ATAN, MPC_IR_SINH, MPC_IR_COSH, MPC_IR_TANH,
+  MPC_IR_COT, MPC_IR_SEC, MPC_IR_CSC, MPC_IR_ASINH, MPC_IR_ACOSH, MPC_IR_ATANH, MPC_IR_COTH, MPC_IR_SECH,
+  MPC_IR_CSCH, MPC_IR_ACOT, MPC_IR_ASEC, MPC_IR_ACSC, MPC_IR_ACOTH, MPC_IR_ASECH, MPC_IR_ACSCH, MPC_IR_ABS,
+  MPC_IR_LOG10, MPC_IR_LOG2, MPC_IR_CBRT, MPC_IR_FLOOR, MPC_IR_CEIL, MPC_IR_ROUND, MPC_IR_SIGN, MPC_IR_TRUNC,
+  MPC_IR_EXPM1, MPC_IR_LOG1P, MPC_IR_ERF,                                                    /* UnaryOp */
+  MPC_IR_ADD = 64, MPC_IR_SUB, MPC_IR_MUL, MPC_IR_DIV, MPC_IR_POW, MPC_IR_ATAN2, MPC_IR_HYPOT, MPC_IR_MIN,
+  MPC_IR_MAX,                                                                                 /* BinaryOp */
+  MPC_IR_LT = 80, MPC_IR_LE, MPC_IR_GT, MPC_IR_GE, MPC_IR_EQ, MPC_IR_NE                      /* CmpOp */
+};
+/* Compiles `code` (n_instr instructions) over n_inputs inputs of the given dtypes (f32, f16, bf16;
+ * at most 16) into *out. */
+int mpc_fused_create(mpc_device *dev, const int32_t *code, int32_t n_instr, const double *consts, int32_t n_consts,
+                     int32_t n_inputs, const int32_t *dtypes, mpc_fused **out);
+/* out (f32, contiguous, `shape`) = the expression over the inputs, each read through element
+ * strides aligned to `shape` (0 on broadcast axes): strides[j * rank + k] for input j, axis k. */
+int mpc_fused_run(mpc_fused *f, const void *const *inputs, int32_t rank, const int64_t *shape,
+                  const int64_t *strides, float *out, mpc_stream s);
+int mpc_fused_destroy(mpc_fused *f);
+/* The CUDA source a program lowers to (validation included; no device needed), written to buf
+ * (NUL-terminated, truncated to cap) with its full length in *len; check_compile != 0 also
+ * compiles it with NVRTC. */
+int mpc_fused_lower(const int32_t *code, int32_t n_instr, const double *consts, int32_t n_consts, int32_t n_inputs,
+                    const int32_t *dtypes, int32_t check_compile, char *buf, size_t cap, size_t *len);
 
 /* ---- multi-GPU: NCCL over NVLink, one rank per process (no reference counterpart) ---------- */
 int mpc_comm_unique_id(void *id128);

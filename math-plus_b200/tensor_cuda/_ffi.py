@@ -16,9 +16,9 @@ _PKG = os.path.dirname(_HERE)
 DEFAULT_LIB = os.path.join(_PKG, "lib", "libmathplus_cuda.so")
 
 # mpc_status
-OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_OOM, ERR_CUDA, ERR_TIMEOUT, ERR_POISONED, ERR_NO_DEVICE, ERR_COMM = range(9)
+OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_OOM, ERR_CUDA, ERR_TIMEOUT, ERR_POISONED, ERR_NO_DEVICE, ERR_COMM, ERR_COMPILE = range(10)
 STATUS_NAMES = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "OOM", 4: "CUDA", 5: "TIMEOUT", 6: "POISONED",
-                7: "NO_DEVICE", 8: "COMM"}
+                7: "NO_DEVICE", 8: "COMM", 9: "COMPILE"}
 # mpc_dtype
 F32, F16, BF16, I32, BOOL = range(5)
 DTYPE_CODES = {"f32": F32, "f16": F16, "bf16": BF16, "i32": I32, "bool": BOOL}
@@ -112,6 +112,12 @@ SIGNATURES = {
     "mpc_cumsum": [_dev, _vp, _i32, _vp, _i32, _i64, _i64, _i64, _vp],
     "mpc_strided_copy": [_dev, _vp, C.POINTER(_i64), _vp, C.POINTER(_i64), _i32, _i32, C.POINTER(_i64), _vp],
     "mpc_sort": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, _vp],
+    "mpc_fused_create": [_dev, C.POINTER(_i32), _i32, C.POINTER(C.c_double), _i32, _i32, C.POINTER(_i32),
+                         C.POINTER(_vp)],
+    "mpc_fused_run": [_vp, C.POINTER(_vp), _i32, C.POINTER(_i64), C.POINTER(_i64), _vp, _vp],
+    "mpc_fused_destroy": [_vp],
+    "mpc_fused_lower": [C.POINTER(_i32), _i32, C.POINTER(C.c_double), _i32, _i32, C.POINTER(_i32), _i32, C.c_char_p,
+                        C.c_size_t, C.POINTER(C.c_size_t)],
     "mpc_gather_rows": [_dev, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, C.POINTER(_i64), _vp],
     "mpc_rope": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, C.c_double, _vp],
     "mpc_geglu": [_dev, _vp, _i32, _vp, _i64, _i64, _vp],

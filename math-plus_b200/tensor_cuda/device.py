@@ -444,6 +444,33 @@ class CudaDevice(ArrayDevice):
         """Waits for all queued work (facade.ts:175); raises MpcError on a kernel-side error."""
         self.device.sync()
 
+    # ---- fusion (tensor-compile IR -> one CUDA kernel; facade.ts:126-164) -----------------------
+    def fuse(self, expr, inputs):
+        """Evaluates a traced element-wise expression (an IRNode dict or a ``Traced``) over
+        ``inputs`` in ONE kernel launch with no intermediate buffers. Inputs are float arrays (or
+        raw backend tensors) that broadcast against each other like NumPy's; the result is a new
+        f32 array of the broadcast shape (a raw tensor when the first input is one)."""
+        from .fusion import fuse
+        if not inputs:
+            raise ValueError(f"{_LABEL} fuse: needs at least one input")
+        arrays = isinstance(inputs[0], DeviceArray)
+        raw = [self._own(x, "fuse") if isinstance(x, DeviceArray) else x for x in inputs]
+        out = fuse(self.backend, expr, raw)
+        return self.wrap(out) if arrays else out
+
+    def compile(self, num_inputs: int, fn):
+        """Traces ``fn`` once over symbolic inputs and returns a function that runs it fused on this
+        device: ``f = dev.compile(2, lambda x, y: x.mul(y).add(1).gelu()); z = f(a, b)``."""
+        from .fusion import Traced
+        node = fn(*[Traced.input(i) for i in range(num_inputs)]).node
+
+        def run(*inputs):
+            if len(inputs) != num_inputs:
+                raise ValueError(f"{_LABEL} compile: expects {num_inputs} input(s), got {len(inputs)}")
+            return self.fuse(node, list(inputs))
+
+        return run
+
     # synchronous conveniences for Python callers
     def from_numpy(self, arr: np.ndarray, dtype: str | None = None) -> DeviceArray:
         """Upload now (no coroutine): ``dtype="bf16"`` rounds float input to bfloat16 (or takes

@@ -9,6 +9,7 @@ math-plus repository); the arithmetic lives in mp_oracle.c.
 from __future__ import annotations
 
 import ctypes as C
+import math
 import os
 import subprocess
 
@@ -348,6 +349,126 @@ def mean_pool(x, mask) -> np.ndarray:
     out = np.empty((B, D), np.float32)
     lib().mp_masked_mean_pool_f32(_ptr(x), B, L, D, _ptr(m), _ptr(out))
     return out
+
+
+# ---- tensor-compile's evaluator (packages/tensor-compile/src/ir.ts) ----------------------
+
+def _js_round(x: float) -> float:
+    """Math.round: nearest integer, ties toward +Infinity, -0 for x in [-0.5, -0]."""
+    if x != x or math.isinf(x):
+        return x
+    f = math.floor(x)
+    r = f + 1.0 if x - f >= 0.5 else float(f)
+    return math.copysign(0.0, x) if r == 0 else r
+
+
+def _js_sign(x: float) -> float:
+    return 1.0 if x > 0 else (-1.0 if x < 0 else x)
+
+
+def _js_pow(a: float, b: float) -> float:
+    """Math.pow: NaN for a NaN exponent and for (+-1) ** (+-Infinity)."""
+    if b != b or (abs(a) == 1.0 and math.isinf(b)):
+        return math.nan
+    try:
+        return math.pow(a, b)
+    except ZeroDivisionError:  # 0 ** negative
+        return math.copysign(math.inf, a) if (b % 2 == 1) else math.inf
+    except (OverflowError, ValueError):
+        return float(np.power(np.float64(a), np.float64(b)))
+
+
+def _safe(fn):
+    """A libm function with IEEE results where Python's math raises (domain -> NaN, overflow -> inf)."""
+    def g(x):
+        try:
+            return fn(x)
+        except ValueError:
+            return math.nan
+        except OverflowError:
+            return math.inf
+    return g
+
+
+def _div(a, b):
+    with np.errstate(all="ignore"):
+        return np.divide(a, b)
+
+
+_UNARY_F64 = {
+    "neg": lambda x: -x,
+    "relu": lambda x: np.where(x > 0, x, 0.0),
+    "sigmoid": lambda x: _div(1.0, 1.0 + _map(math.exp, -x)),
+    "gelu": lambda x: _map(lambda v: lib().mp_gelu_erf(v), x),
+    "gelu_tanh": lambda x: 0.5 * x * (1.0 + _map(math.tanh, 0.7978845608028654 * (x + 0.044715 * x * x * x))),
+    "exp": lambda x: _map(math.exp, x), "log": lambda x: _map(math.log, x), "sqrt": lambda x: _map(math.sqrt, x),
+    "sin": lambda x: _map(math.sin, x), "cos": lambda x: _map(math.cos, x), "tan": lambda x: _map(math.tan, x),
+    "asin": lambda x: _map(math.asin, x), "acos": lambda x: _map(math.acos, x), "atan": lambda x: _map(math.atan, x),
+    "sinh": lambda x: _map(math.sinh, x), "cosh": lambda x: _map(math.cosh, x), "tanh": lambda x: _map(math.tanh, x),
+    "cot": lambda x: _div(1.0, _map(math.tan, x)), "sec": lambda x: _div(1.0, _map(math.cos, x)),
+    "csc": lambda x: _div(1.0, _map(math.sin, x)),
+    "asinh": lambda x: _map(math.asinh, x), "acosh": lambda x: _map(math.acosh, x),
+    "atanh": lambda x: _map(math.atanh, x),
+    "coth": lambda x: _div(1.0, _map(math.tanh, x)), "sech": lambda x: _div(1.0, _map(math.cosh, x)),
+    "csch": lambda x: _div(1.0, _map(math.sinh, x)),
+    "acot": lambda x: _map(math.atan, _div(1.0, x)), "asec": lambda x: _map(math.acos, _div(1.0, x)),
+    "acsc": lambda x: _map(math.asin, _div(1.0, x)),
+    "acoth": lambda x: 0.5 * _map(math.log, _div(x + 1.0, x - 1.0)),
+    "asech": lambda x: _map(math.acosh, _div(1.0, x)), "acsch": lambda x: _map(math.asinh, _div(1.0, x)),
+    "abs": np.abs, "log10": lambda x: _map(math.log10, x), "log2": lambda x: _map(math.log2, x),
+    "cbrt": lambda x: _map(math.cbrt, x), "floor": np.floor, "ceil": np.ceil, "round": lambda x: _map(_js_round, x),
+    "sign": lambda x: _map(_js_sign, x), "trunc": np.trunc, "expm1": lambda x: _map(math.expm1, x),
+    "log1p": lambda x: _map(math.log1p, x), "erf": lambda x: _map(lambda v: lib().mp_erf(v), x),
+}
+
+
+def _map(fn, x):
+    f = np.frompyfunc(_safe(fn), 1, 1)
+    return np.asarray(f(np.asarray(x, np.float64)), np.float64)
+
+
+_BINARY_F64 = {
+    "add": np.add, "sub": np.subtract, "mul": np.multiply, "div": _div,
+    "pow": lambda a, b: np.asarray(np.frompyfunc(_js_pow, 2, 1)(a, b), np.float64),
+    "atan2": lambda a, b: np.asarray(np.frompyfunc(math.atan2, 2, 1)(a, b), np.float64),
+    "hypot": lambda a, b: np.asarray(np.frompyfunc(math.hypot, 2, 1)(a, b), np.float64),
+    "min": lambda a, b: np.where(a <= b, a, b), "max": lambda a, b: np.where(a >= b, a, b),
+}
+_CMP_F64 = {"lt": np.less, "le": np.less_equal, "gt": np.greater, "ge": np.greater_equal, "eq": np.equal,
+            "ne": np.not_equal}
+
+
+def eval_ir(node: dict, inputs) -> np.ndarray:
+    """``CompiledFn.forward`` (packages/tensor-compile/src/index.ts) over ``evalValue``
+    (ir.ts:339-383): every node in f64 on the broadcast inputs with the value formulas of
+    ``unaryValueAndDeriv`` (ir.ts:96-215) and JavaScript's Math semantics; the result rounded once to
+    f32. Transcendentals come from the C library here and from V8's in the reference: they agree to
+    the last place of f64 or within it."""
+    xs = [np.asarray(x, np.float64) for x in inputs]
+    shape = np.broadcast_shapes(*[x.shape for x in xs])
+    xs = [np.broadcast_to(x, shape) for x in xs]
+
+    def ev(n):
+        k = n["kind"]
+        if k == "input":
+            return xs[n["index"]]
+        if k == "const":
+            return np.full(shape, float(n["value"]))
+        if k == "unary":
+            with np.errstate(all="ignore"):
+                return np.asarray(_UNARY_F64[n["op"]](ev(n["arg"])), np.float64)
+        if k == "binary":
+            with np.errstate(all="ignore"):
+                return np.asarray(_BINARY_F64[n["op"]](ev(n["left"]), ev(n["right"])), np.float64)
+        if k == "cmp":
+            return np.where(_CMP_F64[n["op"]](ev(n["left"]), ev(n["right"])), 1.0, 0.0)
+        if k == "select":
+            c = ev(n["cond"])
+            return np.where(c != 0, ev(n["then"]), ev(n["else"]))
+        raise ValueError(n)
+
+    with np.errstate(all="ignore"):
+        return np.asarray(ev(node), np.float64).astype(np.float32)
 
 
 def round_bf16(x) -> np.ndarray:
