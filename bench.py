@@ -633,7 +633,7 @@ def run_ours(args, w):
             roof["nvlink"] = {"bytes_in_per_gpu": nv_bytes, "achieved_gbs": nv_bytes / (ms_step * 1e-3) / 1e9,
                               "peak_gbs": 770.0, "peak_source": "measured peer copy per direction",
                               "target_ms": target_ms, "frac_of_target": target_ms / ms_step}
-        if w.get("dtype") == "f32":
+        if w["kind"] == "gemm" and w.get("dtype") == "f32":
             roof["note"] = "3xTF32 issues 3 tf32 MMAs per product; tf32 dense peak is half of bf16"
         if w["kind"] == "attention" and w["causal"]:
             roof["note"] = "FLOP = causal half of 4*B*H*L^2*D (masked tiles are skipped)"
