@@ -118,7 +118,9 @@ __device__ __forceinline__ void load_rows(const CUtensorMap *map, uint64_t *bar,
   tma_load_4d(map, bar, dst, col, c1, c2, c3);
 }
 
-template <int D>
+// BF: bf16 operands (P is packed as bf16), else f16. A template parameter, not a run-time flag, so
+// that the softmax's inner loops carry no per-element branch on the type.
+template <int D, bool BF>
 __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Maps maps, const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -392,7 +394,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
             const uint32_t e2 = ex2_f16x2(*reinterpret_cast<const uint32_t *>(&x2));
             rs[e & 7] = add_f16x2_to_f32(rs[e & 7], e2);
             uint32_t packed = e2;
-            if (p.dtype == MPC_BF16) {
+            if (BF) {
               const float2 pf = __half22float2(*reinterpret_cast<const __half2 *>(&e2));
               __nv_bfloat162 v2 = __floats2bfloat162_rn(pf.x, pf.y);
               packed = *reinterpret_cast<uint32_t *>(&v2);
@@ -434,7 +436,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
               const float a = __uint_as_float(r[2 * e]) * inv, bb = __uint_as_float(r[2 * e + 1]) * inv;
-              if (p.dtype == MPC_BF16) {
+              if (BF) {
                 __nv_bfloat162 v2 = __floats2bfloat162_rn(a, bb);
                 ow[e] = *reinterpret_cast<uint32_t *>(&v2);
               } else {
@@ -562,15 +564,15 @@ __global__ void attn_generic_kernel(const GenericParams p) {
   if (p.lse && lane == 0) p.lse[row_id] = l > 0.0f ? m + logf(l) : -INFINITY;
 }
 
-template <int D>
+template <int D, bool BF>
 int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
   using C = Cfg<D>;
   static bool configured[64] = {};
   const int ord = dev->ordinal & 63;
   if (!configured[ord]) {
-    MPC_CUDA(dev, cudaFuncSetAttribute(attn_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    MPC_CUDA(dev, cudaFuncSetAttribute(attn_kernel<D, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaFuncAttributes fa;
-    MPC_CUDA(dev, cudaFuncGetAttributes(&fa, attn_kernel<D>));
+    MPC_CUDA(dev, cudaFuncGetAttributes(&fa, attn_kernel<D, BF>));
     // The register split inside the kernel is sized for a 168-register launch; refuse anything else
     // rather than launch a split whose increase could never be granted.
     if (fa.numRegs != 168)
@@ -580,7 +582,7 @@ int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t s
   // Persistent: one CTA per SM (at most), each taking pairs of units until none is left.
   const long long pairs = ((long long)p.n_units + 1) / 2;
   const long long grid = pairs < dev->prop.multiProcessorCount ? pairs : dev->prop.multiProcessorCount;
-  attn_kernel<D><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(maps, p);
+  attn_kernel<D, BF><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(maps, p);
   dev->launches++;
   return check_launch(dev, "attn_kernel");
 }
@@ -696,7 +698,9 @@ int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void 
     return rc;
   p.k_pos = kpos;
   p.v_pos = vpos;
-  return p.D == 128 ? launch_tc<128>(dev, maps, p, st) : launch_tc<64>(dev, maps, p, st);
+  const bool bf = p.dtype == MPC_BF16;
+  if (p.D == 128) return bf ? launch_tc<128, true>(dev, maps, p, st) : launch_tc<128, false>(dev, maps, p, st);
+  return bf ? launch_tc<64, true>(dev, maps, p, st) : launch_tc<64, false>(dev, maps, p, st);
 }
 
 }  // namespace mpc
