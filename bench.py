@@ -365,7 +365,8 @@ def setup_attention(w, dev, torch, g, local, F):
     def launch(ptrs, optr, stream):
         dev.sdpa(desc, ptrs[0], ptrs[1], ptrs[2], None, optr, lse.ptr, stream)
 
-    return [q, k, v], out, launch, f"attn_kernel<D={D}> (2 Q tiles x 128 rows per CTA, 10 warps)"
+    return [q, k, v], out, launch, (f"attn_kernel<D={D}, {w['dtype']}> (persistent: one CTA per SM, 2 Q tiles x 128 "
+                                    "rows per unit, 12 warps)")
 
 
 def setup_nsplit(w, dev, torch, g, local, F, world, pg):
