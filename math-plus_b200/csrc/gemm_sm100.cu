@@ -53,6 +53,8 @@ struct Params {
   int ndst;            // output maps in use (1 unless the product is stored to several matrices)
   const void *resid;   // MPC_EPI_RESIDUAL: [batch, M, N] in the output type, added last
   int resid_vec;       // resid rows start 16-byte aligned (vector loads)
+  void *c_direct;      // non-null: C [batch, M, N] whose rows are not 16-byte aligned, written with
+                       // plain stores from the staged block instead of TMA
 };
 
 // The operand maps and NDST output maps; each 32 x 32 output block is stored through c[0..ndst).
@@ -425,7 +427,30 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
           __syncwarp();
         }
         stage_row(buf, f, p.out_dtype, lane, half);
-        if (!wide || half == 1) {
+        if ((!wide || half == 1) && p.c_direct) {
+          // Row by row from the staged block: the warp writes one row's 32 (f32) or 64 (16-bit)
+          // consecutive outputs per step, undoing the 128-byte swizzle.
+          __syncwarp();
+          const int cs = col0 - 32 * half;
+#pragma unroll 4
+          for (int rr = 0; rr < 32; ++rr) {
+            const int grow = row0 + rr;
+            const uint32_t v = *reinterpret_cast<const uint32_t *>(buf + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4) +
+                                                                   ((lane & 3) << 2));
+            if (grow < p.M) {
+              const size_t rbase = ((size_t)b * p.M + grow) * (size_t)p.N;
+              if (!wide) {
+                if (cs + lane < p.N) static_cast<float *>(p.c_direct)[rbase + cs + lane] = __uint_as_float(v);
+              } else {
+                uint16_t *c16 = static_cast<uint16_t *>(p.c_direct) + rbase;
+                const int c0 = cs + 2 * lane;
+                if (c0 < p.N) c16[c0] = static_cast<uint16_t>(v & 0xffffu);
+                if (c0 + 1 < p.N) c16[c0 + 1] = static_cast<uint16_t>(v >> 16);
+              }
+            }
+          }
+          __syncwarp();  // the block may be staged again
+        } else if (!wide || half == 1) {
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
@@ -725,15 +750,16 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
   Maps maps;
   memset(&maps, 0, sizeof(maps));
   OperandScratch s;
-  Scratch sc;
-  // Output: a padded staging matrix when the row pitch or base is not 16-byte aligned.
+  // Output: TMA stores when the rows are 16-byte aligned; otherwise the epilogue writes the staged
+  // blocks with plain stores (the element alignment suffices) and the map is unused.
   void *cdst = Cout;
   int64_t ldc = N;
   if (((uintptr_t)Cout & 15) || (N * eo) % 16) {
-    ldc = round_up(N, 16 / eo);
-    if ((rc = sc.get(dev, st, (size_t)(batch * M * ldc) * eo))) return rc;
-    cdst = sc.ptr;
+    if ((uintptr_t)Cout % eo) return fail(MPC_ERR_INVALID, "mpc_gemm: C is not aligned to its element size");
+    p.c_direct = Cout;
+    ldc = round_up(N, 16 / eo);  // any valid map: it is never used
   }
+  if (p.c_direct) cdst = reinterpret_cast<void *>((uintptr_t)Cout & ~uintptr_t(15));  // aligned; never stored to
   if ((rc = make_map_3d(&maps.c[0], tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo,
                         128 / (uint32_t)eo, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
@@ -746,10 +772,7 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
     rc = launch<kHalf, true, 256, 4>(dev, maps, p, st);
   else
     rc = launch<kHalf, false, 256, 4>(dev, maps, p, st);
-  if (rc) return rc;
-  if (cdst != Cout)
-    MPC_CUDA(dev, cudaMemcpy2DAsync(Cout, N * eo, cdst, ldc * eo, N * eo, batch * M, cudaMemcpyDeviceToDevice, st));
-  return MPC_OK;
+  return rc;
 }
 
 // The product stored into several row-major matrices at once (row pitch ldc elements, columns
