@@ -573,6 +573,11 @@ def run_ours(args, w):
         local_c.free()
 
     # ---- e2e: through the C ABI from pinned host buffers, copies inside the timed region ----
+    # Every step copies its inputs host -> device, runs the same step and copies its result device ->
+    # host. Streaming order: inputs and the step on the device's stream, the read-back on a second
+    # stream, device buffers double-buffered, so the read-back of step i overlaps the uploads of step
+    # i + 1 (the two copy directions run on separate copy engines). The region ends when the last
+    # read-back has landed in host memory.
     e2e = None
     if args.e2e_steps > 0:
         hins = []
@@ -580,33 +585,58 @@ def run_ours(args, w):
             raw = t.contiguous().view(torch.uint8).reshape(-1)
             h, hp = dev.pinned_array((raw.numel(),), np.uint8)
             h[:] = raw.cpu().numpy()
-            hins.append((h, hp, dev.alloc(h.nbytes)))
+            hins.append((h, hp, [dev.alloc(h.nbytes), dev.alloc(h.nbytes)]))
         hout, hop = dev.pinned_array((out.nbytes,), np.uint8)
+        single_out = w["kind"] in ("nsplit", "gpt2")  # their output buffer is owned by the step itself
+        outs = [out, out] if single_out else [out, dev.alloc(out.nbytes)]
+        s_out = dev.new_stream()
+        done_step = [dev.event(), dev.event()]
+        done_read = [dev.event(), dev.event()]
+        step_no = [0]
 
         def e2e_step():
-            for h, _, d in hins:
-                dev.copy_h2d(d.ptr, h, stream)
-            launch([d.ptr for _, _, d in hins], out.ptr, stream)
-            dev.copy_d2h_into(hout, out.ptr, stream)
+            k = step_no[0] & 1
+            for h, _, dbuf in hins:
+                dev.copy_h2d(dbuf[k].ptr, h, stream)
+            # the step overwrites an output buffer whose earlier read-back must have finished
+            # (an event never recorded counts as complete)
+            dev.wait_event(stream, done_read[k ^ 1] if single_out else done_read[k])
+            launch([dbuf[k].ptr for _, _, dbuf in hins], outs[k].ptr, stream)
+            dev.record(done_step[k], stream)
+            dev.wait_event(s_out, done_step[k])
+            dev.copy_d2h_into(hout, outs[k].ptr, s_out)
+            dev.record(done_read[k], s_out)
+            step_no[0] += 1
 
-        e2e_step()
+        for _ in range(2):
+            e2e_step()
+        dev.stream_sync(s_out)
         dev.stream_sync(stream)
         barrier()
         x0, x1 = dev.event(), dev.event()
         dev.record(x0, stream)
         for _ in range(args.e2e_steps):
             e2e_step()
-        dev.record(x1, stream)
+        dev.wait_event(s_out, done_step[(step_no[0] - 1) & 1])
+        dev.record(x1, s_out)
+        dev.stream_sync(s_out)
         dev.stream_sync(stream)
         barrier()
         ms_e2e = max_over_ranks(dev.elapsed_ms(x0, x1))
         e2e = {"value": job_flop / (ms_e2e / args.e2e_steps * 1e-3) / scale, "unit": unit,
                "h2d_bytes_per_step": int(sum(h.nbytes for h, _, _ in hins)), "d2h_bytes_per_step": int(hout.nbytes),
                "ms_per_step": ms_e2e / args.e2e_steps,
-               "path": "mpc_memcpy_h2d_async per input -> one kernel -> mpc_memcpy_d2h_async, pinned host buffers"}
-        for _, hp, _ in hins:
+               "path": "per step: mpc_memcpy_h2d_async of every input -> the step -> mpc_memcpy_d2h_async of the "
+                       "result into pinned host memory; read-back on a second stream overlapping the next step's "
+                       "uploads (double-buffered device buffers)"}
+        for _, hp, dbuf in hins:
             dev.host_free(hp)
+            for d in dbuf:
+                d.free()
         dev.host_free(hop)
+        if not single_out:
+            outs[1].free()
+        dev.destroy_stream(s_out)
 
     if rank == 0:
         peaks = load_peaks()

@@ -111,6 +111,8 @@ int mpc_device_stream(mpc_device *dev, mpc_stream *s);
 int mpc_event_create(mpc_device *dev, mpc_event *e);
 int mpc_event_destroy(mpc_device *dev, mpc_event e);
 int mpc_event_record(mpc_device *dev, mpc_event e, mpc_stream s);
+/* Work queued on s after this call waits for e's last recording (cross-stream ordering). */
+int mpc_stream_wait_event(mpc_device *dev, mpc_stream s, mpc_event e);
 int mpc_event_elapsed_ms(mpc_device *dev, mpc_event start, mpc_event stop, float *ms);
 /* Waits for all work of the device, then reports any kernel-side error word. */
 int mpc_sync(mpc_device *dev);

@@ -471,6 +471,13 @@ int mpc_event_record(mpc_device *dev, mpc_event e, mpc_stream s) {
   MPC_CUDA(dev, cudaEventRecord(static_cast<cudaEvent_t>(e), stream_of(dev, s)));
   return MPC_OK;
 }
+int mpc_stream_wait_event(mpc_device *dev, mpc_stream s, mpc_event e) {
+  int rc = enter(dev);
+  if (rc) return rc;
+  if (!e) return fail(MPC_ERR_INVALID, "mpc_stream_wait_event: null event");
+  MPC_CUDA(dev, cudaStreamWaitEvent(stream_of(dev, s), static_cast<cudaEvent_t>(e), 0));
+  return MPC_OK;
+}
 int mpc_event_elapsed_ms(mpc_device *dev, mpc_event a, mpc_event b, float *ms) {
   int rc = enter(dev);
   if (rc) return rc;

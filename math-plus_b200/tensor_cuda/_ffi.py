@@ -99,6 +99,7 @@ SIGNATURES = {
     "mpc_event_create": [_dev, C.POINTER(_vp)],
     "mpc_event_destroy": [_dev, _vp],
     "mpc_event_record": [_dev, _vp, _vp],
+    "mpc_stream_wait_event": [_dev, _vp, _vp],
     "mpc_event_elapsed_ms": [_dev, _vp, _vp, C.POINTER(C.c_float)],
     "mpc_sync": [_dev],
     "mpc_launch_count": [_dev, C.POINTER(_u64)],

@@ -147,6 +147,18 @@ class Device:
     def record(self, event: int, stream=None) -> None:
         F.call("mpc_event_record", self.handle, C.c_void_p(event), C.c_void_p(stream))
 
+    def wait_event(self, stream, event: int) -> None:
+        """Orders later work on ``stream`` after ``event``'s last recording."""
+        F.call("mpc_stream_wait_event", self.handle, C.c_void_p(stream), C.c_void_p(event))
+
+    def new_stream(self) -> int:
+        s = C.c_void_p()
+        F.call("mpc_stream_create", self.handle, C.byref(s))
+        return s.value
+
+    def destroy_stream(self, stream: int) -> None:
+        F.call("mpc_stream_destroy", self.handle, C.c_void_p(stream))
+
     def elapsed_ms(self, start: int, stop: int) -> float:
         ms = C.c_float()
         F.call("mpc_event_elapsed_ms", self.handle, C.c_void_p(start), C.c_void_p(stop), C.byref(ms))
