@@ -173,15 +173,31 @@ __global__ void layer_norm_warp_kernel(const uint4 *__restrict__ x, const float 
   const int dv = d / N;
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps) {
-    const uint4 *xr = x + r * dv;
+  int64_t r = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  // Short rows (at most 4 vectors per lane): the warp's next row is loaded while the current one
+  // is normalised. Longer rows already keep enough bytes in flight per warp (and the registers a
+  // second row would take cost occupancy).
+  constexpr bool kAhead = MAXV <= 4;
+  uint4 nxt[MAXV];
+  if (kAhead && r < rows) {
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k)
+      if (lane + 32 * k < dv) nxt[k] = x[r * dv + lane + 32 * k];
+  }
+  for (; r < rows; r += warps) {
     float v[MAXV][N];
+#pragma unroll
+    for (int k = 0; k < MAXV; ++k)
+      if (lane + 32 * k < dv) Vec<T>::load(kAhead ? nxt[k] : x[r * dv + lane + 32 * k], v[k]);
+    if (kAhead && r + warps < rows) {
+#pragma unroll
+      for (int k = 0; k < MAXV; ++k)
+        if (lane + 32 * k < dv) nxt[k] = x[(r + warps) * dv + lane + 32 * k];
+    }
     float s = 0.0f;
 #pragma unroll
     for (int k = 0; k < MAXV; ++k) {
-      const int j = lane + 32 * k;
-      if (j < dv) {
-        Vec<T>::load(xr[j], v[k]);
+      if (lane + 32 * k < dv) {
 #pragma unroll
         for (int e = 0; e < N; ++e) s += v[k][e];
       }
@@ -207,6 +223,74 @@ __global__ void layer_norm_warp_kernel(const uint4 *__restrict__ x, const float 
         float y[N], wv[N], bv[N];
 #pragma unroll
         for (int e = 0; e < N; e += 4) {  // weight / bias rows are f32, 16-byte aligned per vector
+          const float4 a = w ? __ldg(reinterpret_cast<const float4 *>(w + j * N + e)) : make_float4(1, 1, 1, 1);
+          const float4 c = b ? __ldg(reinterpret_cast<const float4 *>(b + j * N + e)) : make_float4(0, 0, 0, 0);
+          wv[e] = a.x, wv[e + 1] = a.y, wv[e + 2] = a.z, wv[e + 3] = a.w;
+          bv[e] = c.x, bv[e + 1] = c.y, bv[e + 2] = c.z, bv[e + 3] = c.w;
+        }
+#pragma unroll
+        for (int e = 0; e < N; ++e) y[e] = (v[k][e] - mean) * inv * wv[e] + bv[e];
+        orow[j] = Vec<T>::store(y);
+      }
+    }
+  }
+}
+
+// Sum over a 256-thread block (8 warps); every thread gets the total.
+__device__ __forceinline__ float block_sum256(float v, float *red) {
+  v = warp_sum(v);
+  const int wi = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[wi] = v;
+  __syncthreads();
+  float t = l < 8 ? red[l] : 0.0f;
+  t = warp_sum(t);
+  __syncthreads();  // red is written again by the next call
+  return t;
+}
+
+// LayerNorm of rows too long for one warp's registers (up to 256 x PER 16-byte vectors): one
+// 256-thread block per row holds the row in registers, so x is read once; block-wide sums.
+template <typename T, int PER>
+__global__ void __launch_bounds__(256) layer_norm_block_kernel(const uint4 *__restrict__ x, const float *__restrict__ w,
+                                                               const float *__restrict__ b, float eps,
+                                                               uint4 *__restrict__ out, int64_t rows, int d) {
+  __shared__ float red[8];
+  constexpr int N = Vec<T>::N;
+  const int dv = d / N;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint4 *xr = x + r * dv;
+    float v[PER][N];
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int j = threadIdx.x + 256 * k;
+      if (j < dv) {
+        Vec<T>::load(xr[j], v[k]);
+#pragma unroll
+        for (int e = 0; e < N; ++e) s += v[k][e];
+      }
+    }
+    const float mean = block_sum256(s, red) / (float)d;
+    float q = 0.0f;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      if (threadIdx.x + 256 * k < dv) {
+#pragma unroll
+        for (int e = 0; e < N; ++e) {
+          const float c = v[k][e] - mean;
+          q += c * c;
+        }
+      }
+    }
+    const float inv = 1.0f / sqrtf(block_sum256(q, red) / (float)d + eps);
+    uint4 *orow = out + r * dv;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int j = threadIdx.x + 256 * k;
+      if (j < dv) {
+        float y[N], wv[N], bv[N];
+#pragma unroll
+        for (int e = 0; e < N; e += 4) {
           const float4 a = w ? __ldg(reinterpret_cast<const float4 *>(w + j * N + e)) : make_float4(1, 1, 1, 1);
           const float4 c = b ? __ldg(reinterpret_cast<const float4 *>(b + j * N + e)) : make_float4(0, 0, 0, 0);
           wv[e] = a.x, wv[e + 1] = a.y, wv[e + 2] = a.z, wv[e + 3] = a.w;
@@ -406,19 +490,30 @@ int mpc_layer_norm(mpc_device *dev, const void *x, int32_t dti, const float *wei
   if (dti == dto && d % vw == 0 && per_lane <= 8 && !(((uintptr_t)x | (uintptr_t)out) & 15) &&
       !(((uintptr_t)weight | (uintptr_t)bias) & 15)) {
     const int64_t blocks_needed = (rows + 7) / 8;  // 8 warps (rows) per 256-thread block
-    const int64_t cap = (int64_t)dev->prop.multiProcessorCount * 16;
-    const unsigned g = (unsigned)(blocks_needed < cap ? blocks_needed : cap);
     const uint4 *xv = static_cast<const uint4 *>(x);
     uint4 *ov = static_cast<uint4 *>(out);
     const int dd = (int)d;
-    // the register footprint follows the row length (fewer registers, more rows in flight)
-#define MPC_LN(T)                                                                                      \
-  switch (per_lane) {                                                                                  \
-    case 1: layer_norm_warp_kernel<T, 1><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
-    case 2: layer_norm_warp_kernel<T, 2><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
-    case 3: layer_norm_warp_kernel<T, 3><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
-    case 4: layer_norm_warp_kernel<T, 4><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
-    default: layer_norm_warp_kernel<T, 8><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd); break; \
+    // One resident wave of blocks (the occupancy of the instantiation); each warp then walks rows,
+    // loading its next row while it normalises the current one. The register footprint follows
+    // the row length (fewer registers, more rows in flight).
+    auto grid_of_ln = [&](const void *kern, bool ahead) -> unsigned {
+      int nb = 16;  // without the next-row load: up to 16 blocks per SM queued
+      if (ahead && (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, 256, 0) != cudaSuccess || nb < 1)) nb = 1;
+      const int64_t cap = (int64_t)dev->prop.multiProcessorCount * nb;
+      return (unsigned)(blocks_needed < cap ? blocks_needed : cap);
+    };
+#define MPC_LN_CASE(T, K)                                                                               \
+  {                                                                                                     \
+    const unsigned g = grid_of_ln(reinterpret_cast<const void *>(layer_norm_warp_kernel<T, K>), K <= 4); \
+    layer_norm_warp_kernel<T, K><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd);               \
+  }
+#define MPC_LN(T)                   \
+  switch (per_lane) {               \
+    case 1: MPC_LN_CASE(T, 1) break; \
+    case 2: MPC_LN_CASE(T, 2) break; \
+    case 3: MPC_LN_CASE(T, 3) break; \
+    case 4: MPC_LN_CASE(T, 4) break; \
+    default: MPC_LN_CASE(T, 8) break; \
   }
     if (dti == MPC_F32) {
       MPC_LN(float)
@@ -428,8 +523,41 @@ int mpc_layer_norm(mpc_device *dev, const void *x, int32_t dti, const float *wei
       MPC_LN(__half)
     }
 #undef MPC_LN
+#undef MPC_LN_CASE
     dev->launches++;
     return check_launch(dev, "layer_norm_warp_kernel");
+  }
+  const int64_t per_thread = (d / vw + 255) / 256;  // 16-byte vectors each thread of a 256-thread block holds
+  if (dti == dto && d % vw == 0 && per_thread <= 8 && d <= INT32_MAX && !(((uintptr_t)x | (uintptr_t)out) & 15) &&
+      !(((uintptr_t)weight | (uintptr_t)bias) & 15)) {
+    const uint4 *xv = static_cast<const uint4 *>(x);
+    uint4 *ov = static_cast<uint4 *>(out);
+    const int dd = (int)d;
+    auto grid_of_lnb = [&](const void *kern) -> unsigned {
+      int nb = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, 256, 0) != cudaSuccess || nb < 1) nb = 1;
+      const int64_t cap = (int64_t)dev->prop.multiProcessorCount * nb;
+      return (unsigned)(rows < cap ? rows : cap);
+    };
+#define MPC_LNB_CASE(T, K)                                                                         \
+  {                                                                                                \
+    const unsigned g = grid_of_lnb(reinterpret_cast<const void *>(layer_norm_block_kernel<T, K>)); \
+    layer_norm_block_kernel<T, K><<<g, 256, 0, st>>>(xv, weight, bias, eps, ov, rows, dd);         \
+  }
+#define MPC_LNB(T)                                                \
+  if (per_thread <= 1) MPC_LNB_CASE(T, 1) else if (per_thread <= 2) MPC_LNB_CASE(T, 2) \
+  else if (per_thread <= 4) MPC_LNB_CASE(T, 4) else MPC_LNB_CASE(T, 8)
+    if (dti == MPC_F32) {
+      MPC_LNB(float)
+    } else if (dti == MPC_BF16) {
+      MPC_LNB(__nv_bfloat16)
+    } else {
+      MPC_LNB(__half)
+    }
+#undef MPC_LNB
+#undef MPC_LNB_CASE
+    dev->launches++;
+    return check_launch(dev, "layer_norm_block_kernel");
   }
   const unsigned grid = (unsigned)(rows < (int64_t)dev->prop.multiProcessorCount * 16 ? rows
                                                                                       : dev->prop.multiProcessorCount * 16);

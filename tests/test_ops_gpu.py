@@ -91,3 +91,29 @@ def test_add_bias_layernorm_embedding_cast(dev):
         _call("mpc_cast", dev.handle, C.c_void_p(dx.ptr), F.F32, C.c_void_p(dc.ptr), F.DTYPE_CODES[dto], x.size, None)
         got = from_device_dtype(dev.download(dc.ptr, dc.nbytes, NP_STORAGE[dto], x.shape), dto)
         assert np.array_equal(got, to_device_dtype(x, dto)[1]), dto
+
+
+@pytest.mark.parametrize("dtype,rows,d", [("f32", 300, 768), ("bf16", 2049, 768), ("f16", 37, 96), ("f32", 70, 2048),
+                                          ("bf16", 500, 4096), ("f16", 33, 8200), ("f32", 9, 5000),
+                                          ("bf16", 3, 30)])
+def test_layer_norm_paths(dev, dtype, rows, d):
+    """Every LayerNorm path: one warp per row (short rows, with the next row loaded ahead), one
+    256-thread block per row held in registers (long rows), and the general kernel (rows whose
+    length is not a multiple of the 16-byte vector): layerNormRows (nn-kernels.ts:108-129), f32
+    statistics, one rounding into the storage type."""
+    from tensor_cuda import _ffi as F
+    x = O.normal_f32(rows * d, 11, 0.5, 2).reshape(rows, d)
+    w = O.normal_f32(d, 12, 1, 0.1)
+    b = O.normal_f32(d, 13, 0, 0.1)
+    xs, xv = to_device_dtype(x, dtype)
+    dx = dev.upload(np.ascontiguousarray(xs))
+    dy = dev.alloc(dx.nbytes)
+    code = {"f32": F.F32, "f16": F.F16, "bf16": F.BF16}[dtype]
+    dw, dbias = dev.upload(w), dev.upload(b)  # kept alive until the kernel has run
+    _call("mpc_layer_norm", dev.handle, C.c_void_p(dx.ptr), code, C.c_void_p(dw.ptr), C.c_void_p(dbias.ptr),
+          C.c_float(1e-5), C.c_void_p(dy.ptr), code, rows, d, None)
+    got = from_device_dtype(dev.download(dy.ptr, dy.nbytes, NP_STORAGE[dtype], xs.shape), dtype).reshape(rows, d)
+    want = O.layer_norm(xv, w, b, 1e-5)
+    _, want_st = to_device_dtype(want, dtype)
+    tol = {"f32": 2e-5, "f16": 2e-3, "bf16": 1.6e-2}[dtype]
+    assert np.abs(got - want_st.reshape(rows, d)).max() <= tol * max(1.0, np.abs(want).max())
