@@ -174,3 +174,20 @@ def test_gemm_residual_epilogue(dev, dtype_in, dtype_out, n, in_place):
     assert np.all(np.abs(got - want) <= gemm_bound(want, absprod + np.abs(r_ex), dtype_in, dtype_out))
     with pytest.raises(F.MpcError, match="mpc_gemm_residual"):
         dev.gemm(desc, da.ptr, dw.ptr, dc.ptr, dbias.ptr)
+
+
+@pytest.mark.parametrize("dtype_out,n", [("bf16", 1001), ("f32", 999), ("f16", 50257 // 7)])
+def test_gemm_unaligned_rows_batched(dev, dtype_out, n):
+    """Outputs whose rows are not 16-byte aligned (the GPT-2 LM head's case) are written by the
+    epilogue with plain stores: batched, with bias + GELU and row / column tails."""
+    from tensor_cuda import _ffi as F
+    bsz, m, k = 3, 150, 64
+    a_up, a_ex = to_device_dtype(O.lcg_gemm(bsz * m * k, 41).reshape(bsz, m, k), "bf16")
+    w_up, w_ex = to_device_dtype(O.lcg_gemm(n * k, 42).reshape(n, k), "bf16")
+    bias = O.normal_f32(n, 43, 0, 0.5)
+    got = run_gemm(dev, a_up, w_up, "bf16", dtype_out, F.B_NK, m, n, k, bias, F.EPI_BIAS | F.EPI_GELU,
+                   batch_shape=(bsz,), a_strides=(m * k,), b_strides=(0,))
+    got = got.reshape(bsz, m, n).astype(np.float64)
+    want = np.stack([O.gelu(O.add_f32(O.linear(a_ex[i], w_ex), bias)) for i in range(bsz)]).astype(np.float64)
+    tol = {"f32": 2e-3, "f16": 4e-3, "bf16": 2e-2}[dtype_out]
+    assert np.all(np.abs(got - want) <= tol * (1 + np.abs(want)))
