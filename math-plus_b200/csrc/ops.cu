@@ -368,6 +368,24 @@ __global__ void embedding_kernel(const void *__restrict__ table, int dt, const i
   }
 }
 
+// The same gather when rows are whole 16-byte vectors: one vector per thread (a GPT-2 token
+// embedding, [32768] ids x 768 bf16, moves 50 MB at the rate of a copy).
+__global__ void embedding_vec_kernel(const uint4 *__restrict__ table, const int32_t *__restrict__ ids,
+                                     uint4 *__restrict__ out, int64_t n_ids, int64_t rows, int64_t dv,
+                                     unsigned long long *bad) {
+  const int64_t total = n_ids * dv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t pos = i / dv, c = i - pos * dv;
+    const int32_t id = ids[pos];
+    if (id < 0 || id >= rows) {
+      if (c == 0) atomicMin(bad, (unsigned long long)pos);
+      out[i] = make_uint4(0, 0, 0, 0);
+    } else {
+      out[i] = table[(int64_t)id * dv + c];
+    }
+  }
+}
+
 __global__ void cast_kernel(const void *__restrict__ x, int dti, void *__restrict__ out, int dto, int64_t n) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     store_from_f32(out, dto, i, load_as_f32(x, dti, i));
@@ -579,10 +597,20 @@ int mpc_embedding(mpc_device *dev, const void *table, int32_t dt, const int32_t 
   Scratch flag;
   if ((rc = flag.get(dev, st, sizeof(unsigned long long)))) return rc;
   MPC_CUDA(dev, cudaMemsetAsync(flag.ptr, 0xff, sizeof(unsigned long long), st));
-  embedding_kernel<<<grid_for(dev, n_ids * d, 256), 256, 0, st>>>(table, dt, ids, out, n_ids, rows, d,
-                                                                  static_cast<unsigned long long *>(flag.ptr));
-  dev->launches++;
-  if ((rc = check_launch(dev, "embedding_kernel"))) return rc;
+  const int64_t row_bytes = d * (int64_t)dtype_size(dt);
+  if (row_bytes % 16 == 0 && !(((uintptr_t)table | (uintptr_t)out) & 15)) {
+    const int64_t dv = row_bytes / 16;
+    embedding_vec_kernel<<<grid_for(dev, n_ids * dv, 256), 256, 0, st>>>(
+        static_cast<const uint4 *>(table), ids, static_cast<uint4 *>(out), n_ids, rows, dv,
+        static_cast<unsigned long long *>(flag.ptr));
+    dev->launches++;
+    if ((rc = check_launch(dev, "embedding_vec_kernel"))) return rc;
+  } else {
+    embedding_kernel<<<grid_for(dev, n_ids * d, 256), 256, 0, st>>>(table, dt, ids, out, n_ids, rows, d,
+                                                                    static_cast<unsigned long long *>(flag.ptr));
+    dev->launches++;
+    if ((rc = check_launch(dev, "embedding_kernel"))) return rc;
+  }
   unsigned long long bad = 0;
   MPC_CUDA(dev, cudaMemcpyAsync(&bad, flag.ptr, sizeof(bad), cudaMemcpyDeviceToHost, st));
   MPC_CUDA(dev, cudaStreamSynchronize(st));

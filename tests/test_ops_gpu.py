@@ -117,3 +117,28 @@ def test_layer_norm_paths(dev, dtype, rows, d):
     _, want_st = to_device_dtype(want, dtype)
     tol = {"f32": 2e-5, "f16": 2e-3, "bf16": 1.6e-2}[dtype]
     assert np.abs(got - want_st.reshape(rows, d)).max() <= tol * max(1.0, np.abs(want).max())
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_embedding_vector_rows(dev, dtype):
+    """Rows of whole 16-byte vectors take the vector gather; an id out of range still reports its
+    first position (takeRows, nn-kernels.ts:277-286)."""
+    from tensor_cuda import _ffi as F
+    V, D = 50, 64
+    table = O.normal_f32(V * D, 21, 0, 1).reshape(V, D)
+    up, ex = to_device_dtype(table, dtype)
+    ids = np.array([[3, 0, 49, 7], [7, 7, 1, 12]], np.int32)
+    dt, di = dev.upload(np.ascontiguousarray(up)), dev.upload(ids)
+    code = {"f32": F.F32, "bf16": F.BF16}[dtype]
+    eb = F.DTYPE_BYTES[code]
+    do = dev.alloc(ids.size * D * eb)
+    bad = C.c_int64()
+    _call("mpc_embedding", dev.handle, C.c_void_p(dt.ptr), code, C.c_void_p(di.ptr), C.c_void_p(do.ptr), ids.size,
+          V, D, C.byref(bad), None)
+    got = from_device_dtype(dev.download(do.ptr, do.nbytes, NP_STORAGE[dtype], (ids.size * D,)), dtype)
+    assert np.array_equal(got.reshape(ids.size, D), ex.reshape(V, D)[ids.reshape(-1)])
+    ids_bad = np.array([1, 2, 50, 3, -1], np.int32)
+    dib = dev.upload(ids_bad)
+    rc = F.load().mpc_embedding(dev.handle, C.c_void_p(dt.ptr), code, C.c_void_p(dib.ptr), C.c_void_p(do.ptr),
+                                ids_bad.size, V, D, C.byref(bad), None)
+    assert rc == F.ERR_INVALID and bad.value == 2
