@@ -88,6 +88,11 @@ def parse_args():
     ap.add_argument("--batch", type=int, default=None, help="override the per-rank batch (small profiling cases)")
     ap.add_argument("--elements", type=int, default=None,
                     help="override the element count of the fused element-wise workload (small profiling cases)")
+    ap.add_argument("--expression", default="sigmoid_chain", choices=sorted(EXPRESSIONS),
+                    help="the fused element-wise workload's expression")
+    ap.add_argument("--precision", default="f64", choices=["f64", "f32"],
+                    help="the fused element-wise workload's evaluation precision (f64: the CPU evaluator's "
+                         "numbers; f32: the WebGPU backend's)")
     return ap.parse_args()
 
 
@@ -183,10 +188,19 @@ def unit_of(w):
     return (w["unit"], 1e9) if w.get("unit") == "GB/s" else ("TFLOP/s", 1e12)
 
 
-def fusion_expr():
+# The fused element-wise workload's expressions over inputs x, y, z: the reference's fused chain
+# (fusion.test.ts:157-163), and an exact-GELU chain whose cost is the erf evaluation.
+EXPRESSIONS = {
+    "sigmoid_chain": ("relu(sigmoid((x + y) * z))", lambda x, y, z: x.add(y).mul(z).sigmoid().relu()),
+    "gelu_chain": ("gelu(x * y + 1) + z", lambda x, y, z: x.mul(y).add(1).gelu().add(z)),
+}
+
+
+def fusion_expr(w=None):
     sys.path.insert(0, os.path.join(ROOT, "math-plus_b200"))
     from tensor_cuda.fusion import Traced
-    return Traced.input(0).add(Traced.input(1)).mul(Traced.input(2)).sigmoid().relu()
+    name = (w or {}).get("expression", "sigmoid_chain")
+    return EXPRESSIONS[name][1](Traced.input(0), Traced.input(1), Traced.input(2))
 
 
 def flop_per_step(w):
@@ -214,18 +228,18 @@ def cpu_sample_rate(w: dict, target_s: float, threads: int):
     import oracle as O
     rng = np.random.default_rng(7)
     if w["kind"] == "fusion":
-        node = fusion_expr().node
+        node = fusion_expr(w).node
         n = 1 << 16
         while True:
             xs = [rng.standard_normal(n).astype(np.float32) for _ in range(3)]
             t0 = time.perf_counter()
-            O.eval_ir(node, xs)
+            O.eval_ir(node, xs, w.get("precision", "f64"))
             dt = time.perf_counter() - t0
             if dt >= target_s / 4 or n >= w["n"]:
                 break
             n = min(w["n"], n * 4)
         return 16.0 * n / dt, (f"{n} of the {w['n']} elements through the oracle's restatement of "
-                               "tensor-compile's evaluator (evalValue, f64, one thread)"), dt
+                               f"tensor-compile's evaluator (evalValue, {w.get('precision', 'f64')}, one thread)"), dt
     if w["kind"] == "gpt2":
         sys.path.insert(0, os.path.join(ROOT, "math-plus_b200"))
         from tensor_cuda.gpt2 import GPT2Config, random_weights
@@ -398,12 +412,13 @@ def setup_fusion(w, dev, torch, g, local, F):
     n = w["n"]
     ins = [torch.randn((n,), generator=g, device=f"cuda:{local}") for _ in range(3)]
     out = dev.alloc(4 * n)
-    k = kernel_for(dev, fusion_expr().node, ["f32"] * 3)
+    k = kernel_for(dev, fusion_expr(w).node, ["f32"] * 3, w.get("precision", "f64"))
 
     def launch(ptrs, optr, stream):
         k.run(ptrs, [(n,)] * 3, (n,), optr, stream)
 
-    return ins, out, launch, "mpc_fused_flat (NVRTC-compiled for sm_100a: 16-byte loads, f64 evaluation)"
+    return ins, out, launch, (f"mpc_fused_flat (NVRTC-compiled for sm_100a: 16-byte loads, "
+                              f"{w.get('precision', 'f64')} evaluation)")
 
 
 def setup_gpt2(w, dev, torch, g, local, F, rank):
@@ -686,7 +701,8 @@ def run_ours(args, w):
             cfg["breakdown_ms_per_step"] = breakdown
         cfg.update({k: w[k] for k in ("batch", "m", "n", "k", "heads", "seq", "head_dim", "out") if k in w})
         if w["kind"] == "fusion":
-            cfg["expression"] = "relu(sigmoid((x + y) * z))"
+            cfg["expression"] = EXPRESSIONS[w.get("expression", "sigmoid_chain")][0]
+            cfg["precision"] = w.get("precision", "f64")
         cfg["l2"] = "flushed between steps (256 MiB write)" if flush is not None else "inputs larger than L2 (126 MB)"
         line = {
             "metric": w["metric"], "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
@@ -725,8 +741,15 @@ def main():
     w = dict(WORKLOADS[args.workload])
     if args.batch is not None:
         w["batch"] = args.batch
-    if args.elements is not None and w["kind"] == "fusion":
-        w["n"] = args.elements
+    if w["kind"] == "fusion":
+        if args.elements is not None:
+            w["n"] = args.elements
+        w["expression"], w["precision"] = args.expression, args.precision
+        if (args.expression, args.precision) != ("sigmoid_chain", "f64"):
+            text = EXPRESSIONS[args.expression][0]
+            w["metric"] = f"fused element-wise GB/s ({text}, f32, {args.precision} evaluation)"
+            w["desc"] = (f"one fused kernel over three f32 inputs of {w['n']} elements: {text}, "
+                         f"{args.precision} evaluation, f32 out (16 bytes per element)")
     if args.impl == "reference":
         run_reference(args, w)
     else:

@@ -299,19 +299,27 @@ enum {
   MPC_IR_LT = 80, MPC_IR_LE, MPC_IR_GT, MPC_IR_GE, MPC_IR_EQ, MPC_IR_NE                      /* CmpOp */
 };
 /* Compiles `code` (n_instr instructions) over n_inputs inputs of the given dtypes (f32, f16, bf16;
- * at most 16) into *out. */
+ * at most 16) into *out. The expression is evaluated in f64 (the reference's JavaScript numbers)
+ * and rounded once to the f32 output. */
 int mpc_fused_create(mpc_device *dev, const int32_t *code, int32_t n_instr, const double *consts, int32_t n_consts,
                      int32_t n_inputs, const int32_t *dtypes, mpc_fused **out);
+/* Evaluate in f32 (the WebGPU backend's WGSL arithmetic) instead of f64: every intermediate value
+ * is rounded to f32, the math functions are their single-precision versions. */
+#define MPC_FUSED_F32 1u
+/* mpc_fused_create with MPC_FUSED_* flags. */
+int mpc_fused_create_ex(mpc_device *dev, const int32_t *code, int32_t n_instr, const double *consts,
+                        int32_t n_consts, int32_t n_inputs, const int32_t *dtypes, uint32_t flags, mpc_fused **out);
 /* out (f32, contiguous, `shape`) = the expression over the inputs, each read through element
  * strides aligned to `shape` (0 on broadcast axes): strides[j * rank + k] for input j, axis k. */
 int mpc_fused_run(mpc_fused *f, const void *const *inputs, int32_t rank, const int64_t *shape,
                   const int64_t *strides, float *out, mpc_stream s);
 int mpc_fused_destroy(mpc_fused *f);
-/* The CUDA source a program lowers to (validation included; no device needed), written to buf
- * (NUL-terminated, truncated to cap) with its full length in *len; check_compile != 0 also
- * compiles it with NVRTC. */
+/* The CUDA source a program lowers to under MPC_FUSED_* flags (validation included; no device
+ * needed), written to buf (NUL-terminated, truncated to cap) with its full length in *len;
+ * check_compile != 0 also compiles it with NVRTC. */
 int mpc_fused_lower(const int32_t *code, int32_t n_instr, const double *consts, int32_t n_consts, int32_t n_inputs,
-                    const int32_t *dtypes, int32_t check_compile, char *buf, size_t cap, size_t *len);
+                    const int32_t *dtypes, uint32_t flags, int32_t check_compile, char *buf, size_t cap,
+                    size_t *len);
 
 /* ---- multi-GPU: NCCL over NVLink, one rank per process (no reference counterpart) ---------- */
 int mpc_comm_unique_id(void *id128);

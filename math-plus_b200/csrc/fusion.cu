@@ -222,31 +222,31 @@ struct MpcFusedParams {
   i64 st[16][6];
   float *out;
 };
-__device__ __forceinline__ double ld_f32(const void *p, i64 i) { return (double)((const float *)p)[i]; }
-__device__ __forceinline__ double ld_f16(const void *p, i64 i) {
+__device__ __forceinline__ real ld_f32(const void *p, i64 i) { return (real)((const float *)p)[i]; }
+__device__ __forceinline__ real ld_f16(const void *p, i64 i) {
   unsigned short h = ((const unsigned short *)p)[i];
   float f;
   asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
-  return (double)f;
+  return (real)f;
 }
-__device__ __forceinline__ double ld_bf16(const void *p, i64 i) {
-  return (double)__uint_as_float(((unsigned int)((const unsigned short *)p)[i]) << 16);
+__device__ __forceinline__ real ld_bf16(const void *p, i64 i) {
+  return (real)__uint_as_float(((unsigned int)((const unsigned short *)p)[i]) << 16);
 }
-__device__ __forceinline__ double h2d(unsigned int h) {
+__device__ __forceinline__ real h2d(unsigned int h) {
   float f;
   asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"((unsigned short)h));
-  return (double)f;
+  return (real)f;
 }
-__device__ __forceinline__ double b2d(unsigned int b) { return (double)__uint_as_float(b << 16); }
-__device__ __forceinline__ void ld4_f32(const void *p, i64 q, double (&v)[4]) {
+__device__ __forceinline__ real b2d(unsigned int b) { return (real)__uint_as_float(b << 16); }
+__device__ __forceinline__ void ld4_f32(const void *p, i64 q, real (&v)[4]) {
   const float4 t = ((const float4 *)p)[q];
   v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
 }
-__device__ __forceinline__ void ld4_f16(const void *p, i64 q, double (&v)[4]) {
+__device__ __forceinline__ void ld4_f16(const void *p, i64 q, real (&v)[4]) {
   const uint2 t = ((const uint2 *)p)[q];
   v[0] = h2d(t.x & 0xffffu); v[1] = h2d(t.x >> 16); v[2] = h2d(t.y & 0xffffu); v[3] = h2d(t.y >> 16);
 }
-__device__ __forceinline__ void ld4_bf16(const void *p, i64 q, double (&v)[4]) {
+__device__ __forceinline__ void ld4_bf16(const void *p, i64 q, real (&v)[4]) {
   const uint2 t = ((const uint2 *)p)[q];
   v[0] = b2d(t.x & 0xffffu); v[1] = b2d(t.x >> 16); v[2] = b2d(t.y & 0xffffu); v[3] = b2d(t.y >> 16);
 }
@@ -256,13 +256,24 @@ __device__ __forceinline__ double js_round(double x) {
   double r = (x - f >= 0.5) ? f + 1.0 : f;
   return r == 0.0 ? copysign(0.0, x) : r;
 }
+__device__ __forceinline__ float js_round(float x) {
+  float f = floorf(x);
+  float r = (x - f >= 0.5f) ? f + 1.0f : f;
+  return r == 0.0f ? copysignf(0.0f, x) : r;
+}
 // Math.sign: NaN stays NaN, a zero keeps its sign.
 __device__ __forceinline__ double js_sign(double x) { return x > 0.0 ? 1.0 : (x < 0.0 ? -1.0 : x); }
+__device__ __forceinline__ float js_sign(float x) { return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : x); }
 // Math.pow: NaN for a NaN exponent and for (+-1) ** (+-Infinity), where C's pow gives 1.
 __device__ __forceinline__ double js_pow(double l, double r) {
   if (r != r) return __longlong_as_double(0x7ff8000000000000LL);
   if (fabs(l) == 1.0 && isinf(r)) return __longlong_as_double(0x7ff8000000000000LL);
   return pow(l, r);
+}
+__device__ __forceinline__ float js_pow(float l, float r) {
+  if (r != r) return __int_as_float(0x7fc00000);
+  if (fabsf(l) == 1.0f && isinf(r)) return __int_as_float(0x7fc00000);
+  return powf(l, r);
 }
 )";
 
@@ -308,13 +319,50 @@ int validate(const int32_t *code, int32_t n_instr, int32_t n_consts, int32_t n_i
 
 std::string temp(int i) { return "t" + std::to_string(i); }
 
-// CUDA source for a validated program: an eval function over the inputs' f64 values and the two
-// kernels around it.
+// A formula for f32 evaluation: the math functions' float versions and float literals.
+std::string to_f32(const std::string &e) {
+  static const char *kFns[] = {"exp", "log", "sqrt", "sin", "cos", "tan", "asin", "acos", "atan", "sinh", "cosh",
+                               "tanh", "asinh", "acosh", "atanh", "fabs", "log10", "log2", "cbrt", "floor", "ceil",
+                               "trunc", "expm1", "log1p", "erf", "normcdf", "atan2", "hypot"};
+  std::string out;
+  size_t i = 0;
+  while (i < e.size()) {
+    const char ch = e[i];
+    if (isalpha((unsigned char)ch) || ch == '_') {  // an identifier
+      size_t j = i;
+      while (j < e.size() && (isalnum((unsigned char)e[j]) || e[j] == '_')) ++j;
+      std::string id = e.substr(i, j - i);
+      if (j < e.size() && e[j] == '(')
+        for (const char *f : kFns)
+          if (id == f) {
+            id += 'f';
+            break;
+          }
+      out += id;
+      i = j;
+    } else if (isdigit((unsigned char)ch)) {  // a number: decimal literals become float literals
+      size_t j = i;
+      bool dot = false;
+      while (j < e.size() && (isdigit((unsigned char)e[j]) || e[j] == '.')) dot |= e[j++] == '.';
+      out += e.substr(i, j - i);
+      if (dot) out += 'f';
+      i = j;
+    } else {
+      out += ch;
+      ++i;
+    }
+  }
+  return out;
+}
+
+// CUDA source for a validated program: an eval function over the inputs' values (f64, or f32 with
+// MPC_FUSED_F32) and the kernels around it.
 std::string lower(const int32_t *code, int32_t n_instr, const double *consts, int32_t n_inputs,
-                  const int32_t *dtypes) {
-  std::string s = kPrelude;
-  s += "__device__ __forceinline__ double mpc_eval(";
-  for (int j = 0; j < n_inputs; ++j) s += (j ? ", double x" : "double x") + std::to_string(j);
+                  const int32_t *dtypes, bool f32) {
+  std::string s = f32 ? "typedef float real;\n" : "typedef double real;\n";
+  s += kPrelude;
+  s += "__device__ __forceinline__ real mpc_eval(";
+  for (int j = 0; j < n_inputs; ++j) s += (j ? ", real x" : "real x") + std::to_string(j);
   s += ") {\n";
   for (int i = 0; i < n_instr; ++i) {
     const int32_t op = code[4 * i], a = code[4 * i + 1], b = code[4 * i + 2], c = code[4 * i + 3];
@@ -325,7 +373,8 @@ std::string lower(const int32_t *code, int32_t n_instr, const double *consts, in
       uint64_t bits;
       memcpy(&bits, &consts[a], sizeof bits);
       char buf[64];
-      snprintf(buf, sizeof buf, "__longlong_as_double(0x%016" PRIx64 "LL)", bits);
+      snprintf(buf, sizeof buf, f32 ? "(float)__longlong_as_double(0x%016" PRIx64 "LL)"
+                                     : "__longlong_as_double(0x%016" PRIx64 "LL)", bits);
       e = buf;
     } else if (const char *u = unary_formula(op)) {
       e = substitute(u, temp(a), "", "");
@@ -334,7 +383,8 @@ std::string lower(const int32_t *code, int32_t n_instr, const double *consts, in
     } else {  // select: nonzero condition takes `then` (NaN counts as nonzero, as in JavaScript)
       e = "(" + temp(a) + " != 0.0 ? " + temp(b) + " : " + temp(c) + ")";
     }
-    s += "  const double " + temp(i) + " = " + e + ";\n";
+    if (f32 && op != MPC_IR_CONST) e = to_f32(e);
+    s += "  const real " + temp(i) + " = " + e + ";\n";
   }
   s += "  return " + temp(n_instr - 1) + ";\n}\n";
 
@@ -343,7 +393,7 @@ std::string lower(const int32_t *code, int32_t n_instr, const double *consts, in
   for (int j = 0; j < n_inputs; ++j) {
     const std::string ld = loader_of(dtypes[j]), js = std::to_string(j);
     args_flat += (j ? ", " : "") + ld + "(p.in[" + js + "], i)";
-    loads_vec += "      double v" + js + "[4];\n      " + std::string(dtypes[j] == MPC_F32 ? "ld4_f32" : (dtypes[j] == MPC_F16 ? "ld4_f16" : "ld4_bf16")) +
+    loads_vec += "      real v" + js + "[4];\n      " + std::string(dtypes[j] == MPC_F32 ? "ld4_f32" : (dtypes[j] == MPC_F16 ? "ld4_f16" : "ld4_bf16")) +
                  "(p.in[" + js + "], q, v" + js + ");\n";
     for (int u = 0; u < 4; ++u) args_vec[u] += (j ? ", v" : "v") + js + "[" + std::to_string(u) + "]";
     args_strided += (j ? ", " : "") + ld + "(p.in[" + js + "], o[" + js + "] + c * p.st[" + js + "][last])";
@@ -356,19 +406,19 @@ std::string lower(const int32_t *code, int32_t n_instr, const double *consts, in
        "  for (i64 q = (i64)blockIdx.x * 256 + threadIdx.x; q < nv; q += (i64)gridDim.x * 256) {\n" +
        loads_vec +
        "      float4 r;\n"
-       "      r.x = __double2float_rn(mpc_eval(" + args_vec[0] + "));\n"
-       "      r.y = __double2float_rn(mpc_eval(" + args_vec[1] + "));\n"
-       "      r.z = __double2float_rn(mpc_eval(" + args_vec[2] + "));\n"
-       "      r.w = __double2float_rn(mpc_eval(" + args_vec[3] + "));\n"
+       "      r.x = (float)(mpc_eval(" + args_vec[0] + "));\n"
+       "      r.y = (float)(mpc_eval(" + args_vec[1] + "));\n"
+       "      r.z = (float)(mpc_eval(" + args_vec[2] + "));\n"
+       "      r.w = (float)(mpc_eval(" + args_vec[3] + "));\n"
        "      ((float4 *)p.out)[q] = r;\n"
        "  }\n"
        "  if (blockIdx.x == 0)\n"
-       "    for (i64 i = (nv << 2) + threadIdx.x; i < p.n; i += 256) p.out[i] = __double2float_rn(mpc_eval(" + args_flat + "));\n"
+       "    for (i64 i = (nv << 2) + threadIdx.x; i < p.n; i += 256) p.out[i] = (float)(mpc_eval(" + args_flat + "));\n"
        "}\n";
   // Contiguous inputs at any alignment: one element per thread.
   s += "extern \"C\" __global__ void __launch_bounds__(256) mpc_fused_flat1(const MpcFusedParams p) {\n"
        "  for (i64 i = (i64)blockIdx.x * 256 + threadIdx.x; i < p.n; i += (i64)gridDim.x * 256)\n"
-       "    p.out[i] = __double2float_rn(mpc_eval(" + args_flat + "));\n"
+       "    p.out[i] = (float)(mpc_eval(" + args_flat + "));\n"
        "}\n";
   // Broadcasting: tiles of 1024 elements along the last axis; a tile's row offsets are decoded once.
   s += "extern \"C\" __global__ void __launch_bounds__(256) mpc_fused_strided(const MpcFusedParams p) {\n"
@@ -391,7 +441,7 @@ std::string lower(const int32_t *code, int32_t n_instr, const double *consts, in
        "#pragma unroll\n"
        "    for (int u = 0; u < 4; ++u) {\n"
        "      const i64 c = c0 + u * 256 + threadIdx.x;\n"
-       "      if (c < inner) p.out[row * inner + c] = __double2float_rn(mpc_eval(" + args_strided + "));\n"
+       "      if (c < inner) p.out[row * inner + c] = (float)(mpc_eval(" + args_strided + "));\n"
        "    }\n"
        "  }\n"
        "}\n";
@@ -438,10 +488,12 @@ using namespace mpc;
 extern "C" {
 
 int mpc_fused_lower(const int32_t *code, int32_t n_instr, const double *consts, int32_t n_consts, int32_t n_inputs,
-                    const int32_t *dtypes, int32_t check_compile, char *buf, size_t cap, size_t *len) {
+                    const int32_t *dtypes, uint32_t flags, int32_t check_compile, char *buf, size_t cap,
+                    size_t *len) {
   int rc = validate(code, n_instr, n_consts, n_inputs, dtypes);
   if (rc) return rc;
-  const std::string src = lower(code, n_instr, consts, n_inputs, dtypes);
+  if (flags & ~MPC_FUSED_F32) return fail(MPC_ERR_INVALID, "fusion: unknown flags 0x%x", flags);
+  const std::string src = lower(code, n_instr, consts, n_inputs, dtypes, flags & MPC_FUSED_F32);
   if (len) *len = src.size();
   if (buf && cap) {
     const size_t n = src.size() < cap - 1 ? src.size() : cap - 1;
@@ -455,17 +507,18 @@ int mpc_fused_lower(const int32_t *code, int32_t n_instr, const double *consts, 
   return MPC_OK;
 }
 
-int mpc_fused_create(mpc_device *dev, const int32_t *code, int32_t n_instr, const double *consts, int32_t n_consts,
-                     int32_t n_inputs, const int32_t *dtypes, mpc_fused **out) {
+int mpc_fused_create_ex(mpc_device *dev, const int32_t *code, int32_t n_instr, const double *consts,
+                        int32_t n_consts, int32_t n_inputs, const int32_t *dtypes, uint32_t flags, mpc_fused **out) {
   int rc = enter(dev);
   if (rc) return rc;
   if (!out) return fail(MPC_ERR_INVALID, "mpc_fused_create: null output");
   *out = nullptr;
   if ((rc = validate(code, n_instr, n_consts, n_inputs, dtypes))) return rc;
+  if (flags & ~MPC_FUSED_F32) return fail(MPC_ERR_INVALID, "fusion: unknown flags 0x%x", flags);
   const DriverApi &drv = driver();
   if (!drv.ok) return fail(MPC_ERR_UNSUPPORTED, "fusion: the driver's module entry points are unavailable");
   std::string cubin;
-  if ((rc = compile(lower(code, n_instr, consts, n_inputs, dtypes), cubin))) return rc;
+  if ((rc = compile(lower(code, n_instr, consts, n_inputs, dtypes, flags & MPC_FUSED_F32), cubin))) return rc;
   MPC_CUDA(dev, cudaFree(nullptr));  // the device's primary context is current from here on
   auto *f = new mpc_fused;
   f->dev = dev;
@@ -482,6 +535,11 @@ int mpc_fused_create(mpc_device *dev, const int32_t *code, int32_t n_instr, cons
   }
   *out = f;
   return MPC_OK;
+}
+
+int mpc_fused_create(mpc_device *dev, const int32_t *code, int32_t n_instr, const double *consts, int32_t n_consts,
+                     int32_t n_inputs, const int32_t *dtypes, mpc_fused **out) {
+  return mpc_fused_create_ex(dev, code, n_instr, consts, n_consts, n_inputs, dtypes, 0, out);
 }
 
 int mpc_fused_run(mpc_fused *f, const void *const *inputs, int32_t rank, const int64_t *shape,

@@ -21,6 +21,7 @@ STATUS_NAMES = {0: "OK", 1: "INVALID", 2: "UNSUPPORTED", 3: "OOM", 4: "CUDA", 5:
                 7: "NO_DEVICE", 8: "COMM", 9: "COMPILE"}
 # mpc_dtype
 F32, F16, BF16, I32, BOOL = range(5)
+FUSED_F32 = 1  # MPC_FUSED_F32
 DTYPE_CODES = {"f32": F32, "f16": F16, "bf16": BF16, "i32": I32, "bool": BOOL}
 DTYPE_BYTES = {F32: 4, F16: 2, BF16: 2, I32: 4, BOOL: 1}
 EPI_BIAS, EPI_GELU, EPI_RESIDUAL = 1, 2, 4
@@ -115,10 +116,12 @@ SIGNATURES = {
     "mpc_sort": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, _vp],
     "mpc_fused_create": [_dev, C.POINTER(_i32), _i32, C.POINTER(C.c_double), _i32, _i32, C.POINTER(_i32),
                          C.POINTER(_vp)],
+    "mpc_fused_create_ex": [_dev, C.POINTER(_i32), _i32, C.POINTER(C.c_double), _i32, _i32, C.POINTER(_i32),
+                            C.c_uint32, C.POINTER(_vp)],
     "mpc_fused_run": [_vp, C.POINTER(_vp), _i32, C.POINTER(_i64), C.POINTER(_i64), _vp, _vp],
     "mpc_fused_destroy": [_vp],
-    "mpc_fused_lower": [C.POINTER(_i32), _i32, C.POINTER(C.c_double), _i32, _i32, C.POINTER(_i32), _i32, C.c_char_p,
-                        C.c_size_t, C.POINTER(C.c_size_t)],
+    "mpc_fused_lower": [C.POINTER(_i32), _i32, C.POINTER(C.c_double), _i32, _i32, C.POINTER(_i32), C.c_uint32, _i32,
+                        C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)],
     "mpc_gather_rows": [_dev, _vp, _i32, _vp, _vp, _i64, _i64, _i64, _i64, C.POINTER(_i64), _vp],
     "mpc_rope": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, C.c_double, _vp],
     "mpc_geglu": [_dev, _vp, _i32, _vp, _i64, _i64, _vp],

@@ -445,20 +445,22 @@ class CudaDevice(ArrayDevice):
         self.device.sync()
 
     # ---- fusion (tensor-compile IR -> one CUDA kernel; facade.ts:126-164) -----------------------
-    def fuse(self, expr, inputs):
+    def fuse(self, expr, inputs, precision: str = "f64"):
         """Evaluates a traced element-wise expression (an IRNode dict or a ``Traced``) over
         ``inputs`` in ONE kernel launch with no intermediate buffers. Inputs are float arrays (or
         raw backend tensors) that broadcast against each other like NumPy's; the result is a new
-        f32 array of the broadcast shape (a raw tensor when the first input is one)."""
+        f32 array of the broadcast shape (a raw tensor when the first input is one). The
+        expression is evaluated in f64 and rounded once (the CPU backend's evaluator), or with
+        ``precision="f32"`` in f32 throughout (the WebGPU backend's WGSL kernels)."""
         from .fusion import fuse
         if not inputs:
             raise ValueError(f"{_LABEL} fuse: needs at least one input")
         arrays = isinstance(inputs[0], DeviceArray)
         raw = [self._own(x, "fuse") if isinstance(x, DeviceArray) else x for x in inputs]
-        out = fuse(self.backend, expr, raw)
+        out = fuse(self.backend, expr, raw, precision)
         return self.wrap(out) if arrays else out
 
-    def compile(self, num_inputs: int, fn):
+    def compile(self, num_inputs: int, fn, precision: str = "f64"):
         """Traces ``fn`` once over symbolic inputs and returns a function that runs it fused on this
         device: ``f = dev.compile(2, lambda x, y: x.mul(y).add(1).gelu()); z = f(a, b)``."""
         from .fusion import Traced
@@ -467,7 +469,7 @@ class CudaDevice(ArrayDevice):
         def run(*inputs):
             if len(inputs) != num_inputs:
                 raise ValueError(f"{_LABEL} compile: expects {num_inputs} input(s), got {len(inputs)}")
-            return self.fuse(node, list(inputs))
+            return self.fuse(node, list(inputs), precision)
 
         return run
 

@@ -152,17 +152,30 @@ def lower(node, n_inputs: int):
     return np.array(code, np.int32).reshape(-1, 4), np.array(consts, np.float64)
 
 
-def lowered_source(node, n_inputs: int, dtypes=None, check_compile: bool = False) -> str:
+PRECISIONS = {"f64": 0, "f32": F.FUSED_F32}
+
+
+def _flags(precision: str) -> int:
+    """MPC_FUSED_* flags of an evaluation precision: "f64" (the JavaScript numbers of the CPU
+    backend's evaluator, the default) or "f32" (the WebGPU backend's WGSL arithmetic)."""
+    try:
+        return PRECISIONS[precision]
+    except KeyError:
+        raise ValueError(f"fusion: precision must be 'f64' or 'f32', got {precision!r}") from None
+
+
+def lowered_source(node, n_inputs: int, dtypes=None, check_compile: bool = False, precision: str = "f64") -> str:
     """The CUDA source the expression compiles to (no device needed); ``check_compile`` also runs
     NVRTC on it."""
+    flags = _flags(precision)
     code, consts = lower(node, n_inputs)
     dts = (C.c_int32 * n_inputs)(*[F.DTYPE_CODES[d] for d in (dtypes or ["f32"] * n_inputs)])
     n = C.c_size_t(0)
     args = (code.ctypes.data_as(C.POINTER(C.c_int32)), len(code),
             consts.ctypes.data_as(C.POINTER(C.c_double)) if len(consts) else None, len(consts), n_inputs, dts)
-    F.call("mpc_fused_lower", *args, 0, None, 0, C.byref(n))
+    F.call("mpc_fused_lower", *args, flags, 0, None, 0, C.byref(n))
     buf = C.create_string_buffer(n.value + 1)
-    F.call("mpc_fused_lower", *args, 1 if check_compile else 0, buf, n.value + 1, C.byref(n))
+    F.call("mpc_fused_lower", *args, flags, 1 if check_compile else 0, buf, n.value + 1, C.byref(n))
     return buf.value.decode()
 
 
@@ -178,16 +191,16 @@ def broadcast_strides(shape, out_shape):
 
 
 class FusedKernel:
-    """One compiled expression for one device and one tuple of input dtypes."""
+    """One compiled expression for one device, one tuple of input dtypes and one precision."""
 
-    def __init__(self, device, code: np.ndarray, consts: np.ndarray, dtypes):
+    def __init__(self, device, code: np.ndarray, consts: np.ndarray, dtypes, precision: str = "f64"):
         self.device = device
         self.n_inputs = len(dtypes)
         dts = (C.c_int32 * self.n_inputs)(*[F.DTYPE_CODES[d] for d in dtypes])
         h = C.c_void_p()
-        F.call("mpc_fused_create", device.handle, code.ctypes.data_as(C.POINTER(C.c_int32)), len(code),
+        F.call("mpc_fused_create_ex", device.handle, code.ctypes.data_as(C.POINTER(C.c_int32)), len(code),
                consts.ctypes.data_as(C.POINTER(C.c_double)) if len(consts) else None, len(consts), self.n_inputs,
-               dts, C.byref(h))
+               dts, _flags(precision), C.byref(h))
         self.handle = h
 
     def run(self, ptrs, shapes, out_shape, out_ptr, stream=None) -> None:
@@ -209,20 +222,23 @@ _cache: dict = {}
 _lock = threading.Lock()
 
 
-def kernel_for(device, node, dtypes) -> FusedKernel:
-    """The compiled kernel of ``node`` for ``device`` and these input dtypes (compiled once)."""
+def kernel_for(device, node, dtypes, precision: str = "f64") -> FusedKernel:
+    """The compiled kernel of ``node`` for ``device``, these input dtypes and this precision
+    (compiled once)."""
+    _flags(precision)
     code, consts = lower(node, len(dtypes))
-    key = (id(device), code.tobytes(), consts.tobytes(), tuple(dtypes))
+    key = (id(device), code.tobytes(), consts.tobytes(), tuple(dtypes), precision)
     with _lock:
         k = _cache.get(key)
         if k is None:
-            k = _cache[key] = FusedKernel(device, code, consts, dtypes)
+            k = _cache[key] = FusedKernel(device, code, consts, dtypes, precision)
     return k
 
 
-def fuse(backend, expr, inputs):
+def fuse(backend, expr, inputs, precision: str = "f64"):
     """Backend-level fusion: ``expr`` over backend tensors ``inputs`` (float dtypes), broadcast
-    against each other; a new f32 tensor of the broadcast shape."""
+    against each other; a new f32 tensor of the broadcast shape. ``precision`` "f64" evaluates as
+    the CPU backend's evaluator does, "f32" as the WebGPU backend's WGSL kernels do."""
     node = expr.node if isinstance(expr, Traced) else expr
     if not inputs:
         raise ValueError("fuse: needs at least one input")
@@ -238,7 +254,7 @@ def fuse(backend, expr, inputs):
         raise ValueError(f"fuse: shapes {[list(t.shape) for t in inputs]} do not broadcast") from e
     if len(out_shape) > 6:
         raise ValueError(f"fuse: rank {len(out_shape)} (at most 6)")
-    k = kernel_for(backend.device, node, [t.dtype for t in inputs])
+    k = kernel_for(backend.device, node, [t.dtype for t in inputs], precision)
     out = backend._alloc(out_shape, "f32")
     if out.size:
         k.run([t.ptr for t in inputs], [tuple(t.shape) for t in inputs], out_shape, out._buf.ptr)

@@ -438,17 +438,30 @@ _CMP_F64 = {"lt": np.less, "le": np.less_equal, "gt": np.greater, "ge": np.great
             "ne": np.not_equal}
 
 
-def eval_ir(node: dict, inputs) -> np.ndarray:
+def eval_ir(node: dict, inputs, precision: str = "f64") -> np.ndarray:
     """``CompiledFn.forward`` (packages/tensor-compile/src/index.ts) over ``evalValue``
     (ir.ts:339-383): every node in f64 on the broadcast inputs with the value formulas of
     ``unaryValueAndDeriv`` (ir.ts:96-215) and JavaScript's Math semantics; the result rounded once to
     f32. Transcendentals come from the C library here and from V8's in the reference: they agree to
-    the last place of f64 or within it."""
+    the last place of f64 or within it.
+
+    ``precision="f32"`` models an f32 evaluation (the WebGPU backend's WGSL kernels,
+    packages/tensor-webgpu/src/fusion-wgsl.ts, compute every node in f32): each node's value is
+    rounded to f32 before its consumers see it. For +, -, *, / and sqrt of f32 operands that is
+    IEEE f32 arithmetic exactly; for the other functions it is the correctly rounded f32 value."""
+    if precision not in ("f64", "f32"):
+        raise ValueError(f"precision must be 'f64' or 'f32', got {precision!r}")
     xs = [np.asarray(x, np.float64) for x in inputs]
     shape = np.broadcast_shapes(*[x.shape for x in xs])
     xs = [np.broadcast_to(x, shape) for x in xs]
+    if precision == "f32":
+        xs = [x.astype(np.float32).astype(np.float64) for x in xs]
 
     def ev(n):
+        v = ev_node(n)
+        return v.astype(np.float32).astype(np.float64) if precision == "f32" else v
+
+    def ev_node(n):
         k = n["kind"]
         if k == "input":
             return xs[n["index"]]

@@ -20,21 +20,22 @@ def unary(op):
 @pytest.mark.parametrize("op", UNARY_OPS)
 def test_every_unary_op_lowers_and_reads_its_input(op):
     src = lowered_source(unary(op), 1)
-    assert "const double t0 = x0;" in src
-    assert "const double t1 = " in src and "t0" in src.split("const double t1 = ")[1].split(";")[0]
+    assert src.startswith("typedef double real;")
+    assert "const real t0 = x0;" in src
+    assert "const real t1 = " in src and "t0" in src.split("const real t1 = ")[1].split(";")[0]
 
 
 @pytest.mark.parametrize("op", BINARY_OPS + CMP_OPS)
 def test_every_binary_and_cmp_op_lowers_with_both_inputs(op):
     t = Traced.input(0).cmp(op, Traced.input(1)) if op in CMP_OPS else getattr(Traced.input(0), op)(Traced.input(1))
-    line = lowered_source(t, 2).split("const double t2 = ")[1].split(";")[0]
+    line = lowered_source(t, 2).split("const real t2 = ")[1].split(";")[0]
     assert "t0" in line and "t1" in line
     if op in CMP_OPS:
         assert "? 1.0 : 0.0" in line
 
 
 def test_select_compares_the_condition_against_zero():
-    line = lowered_source(Traced.input(0).select(Traced.input(1), 2.5), 2).split("const double t3 = ")[1].split(";")[0]
+    line = lowered_source(Traced.input(0).select(Traced.input(1), 2.5), 2).split("const real t3 = ")[1].split(";")[0]
     assert line == "(t0 != 0.0 ? t1 : t2)"
 
 
@@ -85,13 +86,17 @@ def test_the_library_validates_programs():
     code = np.array([[1, 0, 0, 0], [64, 0, 2, 0]], np.int32)  # operand 2 is not earlier
     dts = (C.c_int32 * 1)(F.F32)
     n = C.c_size_t(0)
-    rc = F.load().mpc_fused_lower(code.ctypes.data_as(C.POINTER(C.c_int32)), 2, None, 0, 1, dts, 0, None, 0,
+    rc = F.load().mpc_fused_lower(code.ctypes.data_as(C.POINTER(C.c_int32)), 2, None, 0, 1, dts, 0, 0, None, 0,
                                   C.byref(n))
     assert rc == F.ERR_INVALID and "operands" in F.last_error()
     code = np.array([[1, 0, 0, 0], [99, 0, 0, 0]], np.int32)
-    rc = F.load().mpc_fused_lower(code.ctypes.data_as(C.POINTER(C.c_int32)), 2, None, 0, 1, dts, 0, None, 0,
+    rc = F.load().mpc_fused_lower(code.ctypes.data_as(C.POINTER(C.c_int32)), 2, None, 0, 1, dts, 0, 0, None, 0,
                                   C.byref(n))
     assert rc == F.ERR_INVALID and "unknown op" in F.last_error()
+    code = np.array([[1, 0, 0, 0]], np.int32)
+    rc = F.load().mpc_fused_lower(code.ctypes.data_as(C.POINTER(C.c_int32)), 1, None, 0, 1, dts, 6, 0, None, 0,
+                                  C.byref(n))
+    assert rc == F.ERR_INVALID and "flags" in F.last_error()
 
 
 # ---- the oracle's evaluator (evalValue, ir.ts:339-383) ------------------------------------------
@@ -131,3 +136,48 @@ def test_oracle_matches_closed_forms():
     from scipy.special import erf
     g = O.eval_ir(x.gelu().node, [xs])
     assert np.allclose(g, (0.5 * xs * (1 + erf(xs / np.sqrt(2)))).astype(np.float32), rtol=2e-7, atol=1e-12)
+
+
+# ---- f32 evaluation (the WebGPU backend's precision, fusion-wgsl.ts) ----------------------------
+
+def test_f32_lowering_uses_float_math_and_compiles_every_op():
+    x, y, z = Traced.input(0), Traced.input(1), Traced.input(2)
+    acc = None
+    for op in UNARY_OPS:
+        n = x.gelu("tanh" if op == "gelu_tanh" else "none") if op.startswith("gelu") else getattr(x, op)()
+        acc = n if acc is None else acc.add(n)
+    for op in BINARY_OPS:
+        acc = acc.add(getattr(y, op)(z))
+    for op in CMP_OPS:
+        acc = acc.add(y.cmp(op, z))
+    acc = acc.gt(0).select(acc, x.mul(-1.25))
+    src = lowered_source(acc, 3, ["f32", "f16", "bf16"], check_compile=True, precision="f32")
+    body = src[src.index("mpc_eval("):src.index("return t")]
+    assert src.startswith("typedef float real;")
+    for f in ("expf(", "asinf(", "sinf(", "normcdff(", "fabsf(", "atan2f(", "hypotf(", "log1pf(", "erff("):
+        assert f in body, f
+    assert "asin(" not in body.replace("asinf(", "") and "exp(" not in body.replace("expf(", "")
+    assert "(float)__longlong_as_double(0xbff4000000000000LL)" in body            # -1.25 rounded to f32
+    assert "? 1.0f : 0.0f" in body and "!= 0.0f ?" in body
+    # the default stays f64
+    assert lowered_source(x.exp(), 1).startswith("typedef double real;")
+
+
+def test_precision_is_validated():
+    with pytest.raises(ValueError, match="precision"):
+        lowered_source(Traced.input(0).exp(), 1, precision="f16")
+    with pytest.raises(ValueError, match="precision"):
+        O.eval_ir(Traced.input(0).exp().node, [np.ones(2)], precision="bf16")
+
+
+def test_oracle_f32_rounds_every_node():
+    """(x + 1e-8) - x: f64 keeps the 1e-8, f32 arithmetic loses it for |x| >= 1."""
+    x = Traced.input(0)
+    e = x.add(1e-8).sub(x)
+    v = np.array([1.0, 3.0, -2.0, 1e-9], np.float32)
+    f64 = O.eval_ir(e.node, [v])
+    f32 = O.eval_ir(e.node, [v], precision="f32")
+    assert np.allclose(f64[:3], 1e-8, rtol=1e-6)
+    assert f32[:3].tolist() == [0.0, 0.0, 0.0]
+    v32 = v.astype(np.float32)
+    assert f32[3] == (v32[3] + np.float32(1e-8)) - v32[3]

@@ -213,3 +213,80 @@ def test_unaligned_views_and_collapsed_axes(dev):
     expr = Traced.input(0).sub(Traced.input(1)).div(Traced.input(2))
     got = run(dev, expr, a, b, c)
     assert got.shape == (4, 1, 5, 6, 1) and same_bits(got, O.eval_ir(expr.node, [a, b, c]))
+
+
+# ---- f32 evaluation (precision="f32": every intermediate an f32, as in the WebGPU backend's WGSL,
+# packages/tensor-webgpu/src/fusion-wgsl.ts) ------------------------------------------------------
+
+# CUDA's single-precision functions are within a few units in the last place of the correctly
+# rounded result (the largest documented bound among those used, normcdff, is 5); composite
+# formulas (sigmoid, gelu_tanh, the reciprocal and inverse forms) add a rounding or two.
+F32_ULPS = 16
+
+
+def run32(dev, node, *arrays, dtypes=None):
+    ins = [dev.from_numpy(a, d) for a, d in zip(arrays, dtypes or [None] * len(arrays))]
+    return dev.to_numpy(dev.fuse(node, ins, precision="f32"))
+
+
+@pytest.mark.parametrize("op,domain", UNARY_CASES)
+def test_unary_ops_f32(dev, op, domain):
+    x = random_data(4096, 1, 0.8)
+    data = {"x": x, "pos": np.abs(random_data(4096, 2, 0.8)) + 0.1, "pos1": np.abs(random_data(4096, 2, 0.8)) + 1.1,
+            "big": np.abs(x) + 1.2, "unit": np.abs(x) * 0.9 + 0.05}[domain]
+    node = {"kind": "unary", "op": op, "arg": {"kind": "input", "index": 0}}
+    got, want = run32(dev, node, data), O.eval_ir(node, [data])
+    if op in EXACT_UNARY:
+        assert same_bits(got, want), op
+    else:
+        assert ulps(got, want).max() <= F32_ULPS, (op, int(ulps(got, want).max()))
+    assert np.all(np.abs(got - want) <= 1e-2 * np.maximum(1, np.abs(want)))  # fusion.test.ts:78-85
+
+
+@pytest.mark.parametrize("op", BINARY_OPS)
+def test_binary_ops_f32(dev, op):
+    a = random_data(4096, 3, 3)
+    b = random_data(4096, 4, 3)
+    b[b == 0] = 0.5
+    if op == "pow":
+        a, b = np.abs(random_data(4096, 5, 2)) + 0.1, random_data(4096, 6, 2)
+    node = getattr(Traced.input(0), op)(Traced.input(1)).node
+    got, want = run32(dev, node, a, b), O.eval_ir(node, [a, b])
+    if op in ("add", "sub", "mul", "div", "min", "max"):
+        assert same_bits(got, want), op
+    else:
+        assert ulps(got, want).max() <= F32_ULPS, (op, int(ulps(got, want).max()))
+
+
+def test_f32_arithmetic_is_ieee_f32_step_by_step(dev):
+    """A chain of +, -, *, / and max equals IEEE f32 arithmetic node by node (no contraction into
+    fused multiply-adds), and differs from the f64 evaluation where an intermediate rounds."""
+    x, y, z = Traced.input(0), Traced.input(1), Traced.input(2)
+    a, b, c = random_data(5000, 23, 3), random_data(5000, 24, 3), random_data(5000, 25, 3)
+    e = x.add(y).mul(z).sub(x).div(y.add(3.5)).max(x.mul(0.1)).add(z.mul(z).mul(1.0 / 3.0))
+    assert same_bits(run32(dev, e, a, b, c), O.eval_ir(e.node, [a, b, c], precision="f32"))
+    lost = x.add(1e-8).sub(x)
+    v = np.array([1.0, 3.0, -2.0, 0.75], np.float32)
+    assert run32(dev, lost, v).tolist() == [0.0, 0.0, 0.0, 0.0]
+    assert np.allclose(run(dev, lost, v), 1e-8, rtol=1e-6)
+
+
+def test_f32_special_values_and_half_inputs(dev):
+    v = np.array([-2.5, -0.5, -0.2, 0.5, 2.5, np.nan, -0.0, 0.0, np.inf, -np.inf, 1.0, -1.0], np.float32)
+    w = np.array([np.nan, np.inf, -np.inf, -2.0, 0.5, 1.0, -1.0, np.nan, 0.0, 3.0, np.inf, np.inf], np.float32)
+    x, y = Traced.input(0), Traced.input(1)
+    for t in (x.round(), x.sign(), x.relu(), x.abs(), x.floor(), x.trunc(), x.neg(), x.min(y), x.max(y), x.eq(y),
+              x.ne(y), x.select(y, x), x.div(y), x.sqrt()):
+        assert same_bits(run32(dev, t, v, w), O.eval_ir(t.node, [v, w])), t.node
+    for t in (x.pow(y), x.hypot(y), x.atan2(y)):  # NaN / infinity cases exact, finite results within bounds
+        assert ulps(run32(dev, t, v, w), O.eval_ir(t.node, [v, w])).max() <= F32_ULPS, t.node
+    from _helpers import to_device_dtype
+    (hx, vx), (hy, vy) = to_device_dtype(random_data(5000, 15, 4), "bf16"), to_device_dtype(random_data(5000, 16, 4), "f16")
+    expr = x.mul(y).gelu()
+    assert ulps(run32(dev, expr, hx, hy, dtypes=["bf16", "f16"]), O.eval_ir(expr.node, [vx, vy])).max() <= F32_ULPS
+    # x * y + 1 cancels where x * y is near -1: its f32 rounding is part of the f32 evaluation, so a
+    # composite expression is checked against the oracle's f32 evaluation (every node rounded)
+    f = dev.compile(2, lambda p, q: p.mul(q).add(1).gelu(), precision="f32")
+    a, b = random_data(1000, 17, 2), random_data(1000, 18, 2)
+    got = dev.to_numpy(f(dev.from_numpy(a), dev.from_numpy(b)))
+    assert ulps(got, O.eval_ir(x.mul(y).add(1).gelu().node, [a, b], precision="f32")).max() <= F32_ULPS
