@@ -65,15 +65,17 @@ struct MapsT {
 using Maps = MapsT<1>;
 constexpr int kMaxDst = 8;
 
-template <int KIND, bool B_MN, int BN, int STAGES>
+template <int KIND, bool B_MN, int BN, int STAGES, bool PAIR = false>
 struct Cfg {
-  static constexpr int BM = 128;
+  static constexpr int BM = 128;                   // rows of A / C per CTA
+  static constexpr int TILE_M = PAIR ? 256 : 128;  // rows of one output tile (a CTA pair shares one)
+  static constexpr int BNL = PAIR ? BN / 2 : BN;   // rows of B held by one CTA
   static constexpr int ES = KIND == kHalf ? 2 : 4;  // operand element bytes
   static constexpr int BK = 128 / ES;               // elements in one 128-byte row
   static constexpr int UK = KIND == kHalf ? 16 : 8;  // K of one tcgen05.mma
   static constexpr int KSTEPS = BK / UK;
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES = BNL * 128;
   static constexpr int NOPS = KIND == kHalf ? 1 : 2;
   static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
   static constexpr int EPI_WARPS = 8;
@@ -85,6 +87,7 @@ struct Cfg {
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocation must be a power of two");
   static_assert(!(KIND == kTF32x3 && B_MN), "3xTF32 operands are always K-major");
+  static_assert(!(PAIR && KIND != kHalf), "CTA pairs run the f16 / bf16 kernel only");
 };
 
 __device__ __forceinline__ void tile_coords(const Params &p, int tile, int &b, int &mt, int &nt) {
@@ -225,9 +228,14 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], in
   }
 }
 
-template <int KIND, bool B_MN, int BN, int STAGES, int NDST>
+// PAIR: a cluster of two CTAs computes one 256 x BN tile with M = 256 tensor-core instructions
+// issued by the even CTA. Each CTA loads its 128 rows of A and half of B's BN rows (counting the
+// bytes on the even CTA's `full` barrier), holds its 128 rows of the accumulator in its own tensor
+// memory and runs its own epilogue; the even CTA's MMA commits release both CTAs' slots and
+// accumulators, and both CTAs' epilogue warps release the accumulator on the even CTA.
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST, bool PAIR>
 __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ MapsT<NDST> maps, const Params p) {
-  using C = Cfg<KIND, B_MN, BN, STAGES>;
+  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *stages = smem;
@@ -241,6 +249,9 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0: the CTA that issues the MMAs
+  const int first_tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tile_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -249,7 +260,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], C::EPI_WARPS);
+      mbar_init(&acc_empty[a], C::EPI_WARPS * (PAIR ? 2 : 1));
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -265,13 +276,27 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
     }
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Cluster addresses: the even CTA's `full` and `acc_empty` barriers (where both CTAs count),
+  // and the odd CTA's `empty` and `acc_full` barriers (which the even CTA's commits release).
+  const uint32_t full_lead = PAIR ? cluster_addr(full, 0) : 0;
+  const uint32_t acc_empty_lead = PAIR ? cluster_addr(acc_empty, 0) : 0;
+  const uint32_t empty_odd = PAIR ? cluster_addr(empty, 1) : 0;
+  const uint32_t acc_full_odd = PAIR ? cluster_addr(acc_full, 1) : 0;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -280,10 +305,11 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.tiles_total; tile += gridDim.x) {
+      for (int tile = first_tile; ok && tile < p.tiles_total; tile += tile_step) {
         int b, mt, nt, ia, ib;
         tile_coords(p, tile, b, mt, nt);
         batch_index(p, b, ia, ib);
+        const int m_base = mt * C::TILE_M + static_cast<int>(rank) * C::BM;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitProducer, p.timeout_ns)) {
             ok = false;
@@ -291,8 +317,28 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
           }
           uint8_t *sa = stages + stage * C::STAGE_BYTES;
           uint8_t *sb = sa + C::A_BYTES;
+          if constexpr (PAIR) {
+            // Both CTAs' bytes complete the even CTA's barrier, which the even CTA arms.
+            if (rank == 0) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            const uint32_t bar = full_lead + stage * 8;
+            const int n_base = nt * BN + static_cast<int>(rank) * C::BNL;
+            tma_load_3d_pair(&maps.a, bar, sa, kb * C::BK, m_base, ia);
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int j = 0; j < C::BNL / 64; ++j)
+                tma_load_3d_pair(&maps.b, bar, sb + j * (C::BK * 128), n_base + j * 64, kb * C::BK, ib);
+            } else {
+              tma_load_3d_pair(&maps.b, bar, sb, kb * C::BK, n_base, ib);
+            }
+            ++issued;
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_3d(&maps.a, &full[stage], sa, kb * C::BK, mt * C::BM, ia);
+          tma_load_3d(&maps.a, &full[stage], sa, kb * C::BK, m_base, ia);
           if constexpr (B_MN) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
@@ -303,7 +349,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
           if constexpr (KIND == kTF32x3) {
             uint8_t *sa2 = sb + C::B_BYTES;
             uint8_t *sb2 = sa2 + C::A_BYTES;
-            tma_load_3d(&maps.a_lo, &full[stage], sa2, kb * C::BK, mt * C::BM, ia);
+            tma_load_3d(&maps.a_lo, &full[stage], sa2, kb * C::BK, m_base, ia);
             tma_load_3d(&maps.b_lo, &full[stage], sb2, kb * C::BK, nt * BN, ib);
           }
           ++issued;
@@ -313,9 +359,11 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
           }
         }
       }
-      if (!ok) {
+      if (!ok && !(PAIR && rank == 1)) {
         // Let the copies already in flight land before shared memory goes away: wait on the
-        // full barriers of the (up to STAGES) most recently armed slots.
+        // full barriers of the (up to STAGES) most recently armed slots. (The odd CTA of a pair
+        // counts its bytes on the even CTA's barriers; it gave up only after a full timeout
+        // without a released slot, long after its last copies landed.)
         const int n = issued < STAGES ? issued : STAGES;
         int s = stage;
         uint32_t ph = phase;
@@ -330,14 +378,14 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer (one thread) ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (one thread; the even CTA's for a pair) ----------------
+    if (lane == 0 && rank == 0) {
       const uint32_t idesc_rt = p.idesc;
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < p.tiles_total; tile += gridDim.x, ++local) {
+      for (int tile = first_tile; ok && tile < p.tiles_total; tile += tile_step, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.err, kErrWaitAccEmpty, p.timeout_ns)) break;
@@ -357,7 +405,9 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
             const uint64_t bd = B_MN ? make_sdesc(b_addr + ks * (C::UK * 128), C::BK * 128, 1024)
                                      : make_sdesc(b_addr + ks * (C::UK * C::ES), 16, 1024);
             const uint32_t accum = (kb | ks) ? 1u : 0u;
-            if constexpr (KIND == kHalf) {
+            if constexpr (PAIR) {
+              mma_f16_ss_pair(d_tmem, ad, bd, idesc_rt, accum);
+            } else if constexpr (KIND == kHalf) {
               mma_f16_ss(d_tmem, ad, bd, idesc_rt, accum);
             } else {
               const uint32_t a2 = b_addr + C::B_BYTES;
@@ -369,17 +419,30 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
               mma_tf32_ss(d_tmem, ad, bd, idesc_rt, 1u);      // hi · hi
             }
           }
-          tc_commit(&empty[stage]);  // the slot is free once these MMAs have read it
+          if constexpr (PAIR) {  // the slot is free in both CTAs once these MMAs have read it
+            tc_commit_pair(smem_u32(&empty[stage]));
+            tc_commit_pair(empty_odd + stage * 8);
+          } else {
+            tc_commit(&empty[stage]);  // the slot is free once these MMAs have read it
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(&acc_full[acc]);
+        if constexpr (PAIR) {
+          tc_commit_pair(smem_u32(&acc_full[acc]));
+          tc_commit_pair(acc_full_odd + acc * 8);
+        } else {
+          tc_commit(&acc_full[acc]);
+        }
       }
       // Every MMA this thread issued has completed once `drain` flips.
-      tc_commit(drain);
+      if constexpr (PAIR)
+        tc_commit_pair(smem_u32(drain));
+      else
+        tc_commit(drain);
       volatile int never = 0;
       mbar_wait(drain, 0, &never, p.err, kErrWaitConsumer, p.timeout_ns);
     }
@@ -391,7 +454,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
     const int col_base = (ew >> 2) * COLS;
     uint8_t *buf = epi + ew * 4096;
     int local = 0;
-    for (int tile = blockIdx.x; tile < p.tiles_total; tile += gridDim.x, ++local) {
+    for (int tile = first_tile; tile < p.tiles_total; tile += tile_step, ++local) {
       int b, mt, nt;
       tile_coords(p, tile, b, mt, nt);
       const int acc = local & 1;
@@ -399,7 +462,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
       if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull, p.timeout_ns)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + col_base;
-      const int row0 = mt * C::BM + q * 32;
+      const int row0 = mt * C::TILE_M + static_cast<int>(rank) * C::BM + q * 32;
       uint32_t r[32];
       tmem_ld32(t_row, r);
 #pragma unroll 1
@@ -414,7 +477,12 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
           // This warp's share of the accumulator is in registers: release it to the MMA warp.
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[acc]);
+          if (lane == 0) {
+            if constexpr (PAIR)
+              mbar_arrive_cluster(acc_empty_lead + acc * 8);
+            else
+              mbar_arrive(&acc_empty[acc]);
+          }
         }
         const int col0 = nt * BN + col_base + c * 32;
         epilogue_math(p, f, col0, lane);
@@ -482,10 +550,17 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
   }
 
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  if constexpr (PAIR)
+    cluster_sync();  // neither CTA frees tensor memory or leaves while the other may signal it
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -550,18 +625,44 @@ __global__ void fill_epilogue_kernel(void *C, int out_dtype, int64_t rows, int64
   }
 }
 
-template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1>
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1, bool PAIR = false>
 int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream_t st) {
-  using C = Cfg<KIND, B_MN, BN, STAGES>;
-  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST>;
+  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR>;
+  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST, PAIR>;
   static bool configured[64] = {};
+  static int pairs_resident[64] = {};
   const int ord = dev->ordinal & 63;
   if (!configured[ord]) {
     MPC_CUDA(dev, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     configured[ord] = true;
   }
-  const int grid = p.tiles_total < dev->prop.multiProcessorCount ? p.tiles_total : dev->prop.multiProcessorCount;
-  kern<<<grid, C::THREADS, C::SMEM, st>>>(maps, p);
+  if constexpr (PAIR) {
+    // One persistent pair per TPC that can hold one: as many clusters of two as fit at once.
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (!pairs_resident[ord]) {
+      cfg.gridDim = dim3(2 * (dev->prop.multiProcessorCount / 2));
+      int n = 0;
+      MPC_CUDA(dev, cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      if (n < 1) return fail(MPC_ERR_UNSUPPORTED, "gemm_kernel: no CTA pair fits on this device");
+      pairs_resident[ord] = n;
+    }
+    const int pairs = p.tiles_total < pairs_resident[ord] ? p.tiles_total : pairs_resident[ord];
+    cfg.gridDim = dim3(2 * pairs);
+    MPC_CUDA(dev, cudaLaunchKernelEx(&cfg, kern, maps, p));
+  } else {
+    const int grid = p.tiles_total < dev->prop.multiProcessorCount ? p.tiles_total : dev->prop.multiProcessorCount;
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(maps, p);
+  }
   dev->launches++;
   return check_launch(dev, "gemm_kernel");
 }
@@ -589,12 +690,14 @@ namespace gemm {
 struct Prep {
   int64_t batch = 1, nA = 1, nB = 1;
   bool tf32 = false, b_mn = false;
+  bool pair = false;  // CTA pairs: 256 x 256 tiles, two SMs per tile
   int BN = 256;
 };
 
 // Validates `d` and fills every kernel parameter that does not depend on the output.
 // Returns MPC_OK with prep.batch == 0 (or M / N == 0) when there is nothing to compute.
-static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, const char *who, Params &p, Prep &pr) {
+static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, const char *who, Params &p, Prep &pr,
+                   bool allow_pair = false) {
   const int64_t M = d->m, N = d->n, K = d->k;
   if (M < 0 || N < 0 || K < 0)
     return fail(MPC_ERR_INVALID, "%s: negative dimension m=%lld n=%lld k=%lld", who, (long long)M, (long long)N,
@@ -631,10 +734,14 @@ static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, c
   pr.BN = pr.tf32 ? 128 : 256;
   // 3xTF32 on a problem with fewer 128 x 128 tiles than SMs: 128 x 64 tiles keep more SMs busy.
   if (pr.tf32 && pr.batch * ((M + 127) / 128) * ((N + 127) / 128) < dev->prop.multiProcessorCount) pr.BN = 64;
+  // f16 / bf16 with at least one 256 x 256 tile per resident pair: CTA pairs (half the B bytes
+  // per SM, a third less operand traffic per product than 128 x 256 tiles on one SM).
+  pr.pair = allow_pair && !pr.tf32 &&
+            pr.batch * ((M + 255) / 256) * ((N + 255) / 256) >= dev->prop.multiProcessorCount / 2;
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
-  p.tiles_m = (int)((M + 127) / 128);
+  p.tiles_m = (int)((M + (pr.pair ? 255 : 127)) / (pr.pair ? 256 : 128));
   p.tiles_n = (int)((N + pr.BN - 1) / pr.BN);
   const int64_t tiles = pr.batch * p.tiles_m * p.tiles_n;
   if (tiles > INT32_MAX) return fail(MPC_ERR_UNSUPPORTED, "%s: %lld tiles", who, (long long)tiles);
@@ -644,7 +751,8 @@ static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, c
   p.alpha = d->alpha;
   p.bias = bias;
   p.epilogue = d->epilogue & (MPC_EPI_BIAS | MPC_EPI_GELU | MPC_EPI_RESIDUAL);
-  p.idesc = make_idesc(pr.tf32 ? kFmtTF32 : (d->dtype_in == MPC_BF16 ? kFmtBF16 : kFmtF16), pr.b_mn, 128, pr.BN);
+  p.idesc = make_idesc(pr.tf32 ? kFmtTF32 : (d->dtype_in == MPC_BF16 ? kFmtBF16 : kFmtF16), pr.b_mn,
+                       pr.pair ? 256 : 128, pr.BN);
   p.out_dtype = d->dtype_out;
   p.err = dev->d_err;
   p.timeout_ns = dev->timeout_ns;
@@ -720,7 +828,7 @@ static int operand_maps(mpc_device *dev, const mpc_gemm_desc *d, const Prep &pr,
     MPC_CUDA(dev, cudaMemcpy2DAsync(s.b.ptr, ldb * es, B, K * es, K * es, nB * N, cudaMemcpyDeviceToDevice, st));
     bp = s.b.ptr;
   }
-  return make_map_3d(&maps.b, dt, bp, K, N, nB, ldb * es, N * ldb * es, 64, 256, SW);
+  return make_map_3d(&maps.b, dt, bp, K, N, nB, ldb * es, N * ldb * es, 64, pr.pair ? 128 : 256, SW);
 }
 
 }  // namespace gemm
@@ -730,7 +838,7 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
   using namespace gemm;
   Params p;
   Prep pr;
-  int rc = prepare(dev, d, bias, "mpc_gemm", p, pr);
+  int rc = prepare(dev, d, bias, "mpc_gemm", p, pr, true);
   if (rc) return rc;
   const int64_t M = d->m, N = d->n, K = d->k, batch = pr.batch;
   if ((d->epilogue & MPC_EPI_RESIDUAL) && !resid)
@@ -768,6 +876,10 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
     rc = launch<kTF32x3, false, 64, 4>(dev, maps, p, st);
   else if (pr.tf32)
     rc = launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
+  else if (pr.pair && pr.b_mn)
+    rc = launch<kHalf, true, 256, 6, 1, true>(dev, maps, p, st);
+  else if (pr.pair)
+    rc = launch<kHalf, false, 256, 6, 1, true>(dev, maps, p, st);
   else if (pr.b_mn)
     rc = launch<kHalf, true, 256, 4>(dev, maps, p, st);
   else

@@ -191,3 +191,64 @@ def test_gemm_unaligned_rows_batched(dev, dtype_out, n):
     want = np.stack([O.gelu(O.add_f32(O.linear(a_ex[i], w_ex), bias)) for i in range(bsz)]).astype(np.float64)
     tol = {"f32": 2e-3, "f16": 4e-3, "bf16": 2e-2}[dtype_out]
     assert np.all(np.abs(got - want) <= tol * (1 + np.abs(want)))
+    # the same products through the aligned path (N padded to 16 bytes, TMA stores): every element
+    # has the same K order, so the plain stores must give identical bits, rows of both parities
+    npad = -(-n * (4 if dtype_out == "f32" else 2) // 16) * 16 // (4 if dtype_out == "f32" else 2)
+    w_pad = np.zeros((npad, k), w_up.dtype)
+    w_pad[:n] = w_up
+    ref = run_gemm(dev, a_up, w_pad, "bf16", dtype_out, F.B_NK, m, npad, k, np.pad(bias, (0, npad - n)),
+                   F.EPI_BIAS | F.EPI_GELU, batch_shape=(bsz,), a_strides=(m * k,), b_strides=(0,))
+    assert np.array_equal(got, ref.reshape(bsz, m, npad)[:, :, :n].astype(np.float64))
+
+
+@pytest.mark.parametrize("b_layout,dtype_in,dtype_out,epi,n", [
+    ("nk", "bf16", "f32", "", 2200),
+    ("kn", "f16", "f32", "bias+gelu", 2200),
+    ("nk", "bf16", "bf16", "bias+residual", 2200),
+    ("kn", "bf16", "bf16", "", 2201),     # rows not 16-byte aligned: plain stores
+])
+def test_gemm_cta_pair_tiles(dev, b_layout, dtype_in, dtype_out, epi, n):
+    """Problems with at least one 256 x 256 tile per resident CTA pair run on pairs of SMs (M = 256
+    tensor-core instructions, half of B per SM): batched, with row, column and K tails (M = 2200,
+    K = 200), both B layouts, every epilogue and unaligned output rows, against the oracle."""
+    import ctypes as C
+    from tensor_cuda import _ffi as F
+    from tensor_cuda.runtime import gemm_desc
+    bsz, m, k = 2, 2200, 200
+    lay = F.B_NK if b_layout == "nk" else F.B_KN
+    a_up, a_ex = to_device_dtype(O.lcg_gemm(bsz * m * k, 51).reshape(bsz, m, k), dtype_in)
+    b_shape = (n, k) if b_layout == "nk" else (k, n)
+    b_up, b_ex = to_device_dtype(O.lcg_gemm(bsz * n * k, 52).reshape((bsz,) + b_shape), dtype_in)
+    bias = O.normal_f32(n, 53, 0, 0.5)
+    flags = (F.EPI_BIAS if "bias" in epi else 0) | (F.EPI_GELU if "gelu" in epi else 0)
+    eo = F.DTYPE_BYTES[F.DTYPE_CODES[dtype_out]]
+    desc = gemm_desc(m, n, k, F.DTYPE_CODES[dtype_in], F.DTYPE_CODES[dtype_out], lay,
+                     flags | (F.EPI_RESIDUAL if "residual" in epi else 0), 1.0, (bsz,), (m * k,), (n * k,))
+    da, db, dbias = dev.upload(a_up), dev.upload(b_up), dev.upload(bias)
+    dc = dev.alloc(bsz * m * n * eo)
+    r_ex = None
+    if "residual" in epi:
+        r_up, r_ex = to_device_dtype(O.lcg_gemm(bsz * m * n, 54).reshape(bsz, m, n), dtype_out)
+        dr = dev.upload(r_up)
+        F.call("mpc_gemm_residual", dev.handle, C.byref(desc), C.c_void_p(da.ptr), C.c_void_p(db.ptr),
+               C.c_void_p(dc.ptr), C.c_void_p(dbias.ptr), C.c_void_p(dr.ptr), None)
+    else:
+        dev.gemm(desc, da.ptr, db.ptr, dc.ptr, dbias.ptr if flags else None)
+    dev.sync()
+    got = from_device_dtype(dev.download(dc.ptr, bsz * m * n * eo, NP_STORAGE[dtype_out], (bsz * m * n,)),
+                            dtype_out).reshape(bsz, m, n).astype(np.float64)
+    for i in range(bsz):
+        bt = b_ex[i].T if b_layout == "nk" else b_ex[i]
+        prod = a_ex[i].astype(np.float64) @ bt.astype(np.float64)
+        absprod = np.abs(a_ex[i]).astype(np.float64) @ np.abs(bt).astype(np.float64)
+        want = prod
+        if "bias" in epi:
+            want = want + bias
+        if "gelu" in epi:
+            want = O.gelu(want.astype(np.float32)).astype(np.float64)
+            absprod = absprod + np.abs(bias)
+        if r_ex is not None:
+            want = want + r_ex[i]
+            absprod = absprod + np.abs(r_ex[i]) + np.abs(bias)
+        bound = gemm_bound(want, absprod, dtype_in, dtype_out) + (1e-5 * (1 + np.abs(want)) if "gelu" in epi else 0)
+        assert np.all(np.abs(got[i] - want) <= bound), i
