@@ -362,7 +362,8 @@ def setup_gemm(w, dev, torch, g, local, F):
     def launch(ptrs, optr, stream):
         dev.gemm(desc, ptrs[0], ptrs[1], optr, ptrs[2] if epi else None, stream)
 
-    kernel = ("gemm_kernel<kHalf, B MN-major, BN=256, 4 stages, 10 warps>" if w["dtype"] != "f32"
+    kernel = ("gemm_kernel<kHalf, B MN-major, 256 x 256 tiles on CTA pairs (cta_group::2), 6 stages, 10 warps>"
+              if w["dtype"] != "f32"
               else "gemm_kernel<kTF32x3, BN=128, 3 stages> (+ tf32 split prologue)")
     return ins, out, launch, kernel
 
