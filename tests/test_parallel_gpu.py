@@ -55,6 +55,34 @@ def test_multi_store_writes_every_destination_at_its_offset(dev, dtype_in, dtype
         assert np.all(raw[:, :off * eo] == 0x5A) and np.all(raw[:, (off + n) * eo:] == 0x5A)
 
 
+@pytest.mark.parametrize("layout", ["kn", "nk"])
+def test_multi_store_cta_pairs(dev, layout):
+    """A product with at least one 256 x 256 tile per resident CTA pair takes the paired kernel
+    (as the column-split workload's shards do): every destination gets the block, the columns
+    around it stay untouched."""
+    from tensor_cuda import _ffi as F
+    from tensor_cuda.parallel import gemm_multi_store
+    from tensor_cuda.runtime import gemm_desc
+    m, n, k, ldc, off, ndst = 2200, 2304, 200, 6912, 2304, 2
+    a, ea = to_device_dtype(O.lcg_gemm(m * k, 5).reshape(m, k), "bf16")
+    bmat = O.lcg_gemm(k * n, 6).reshape(k, n)
+    b, eb = to_device_dtype(bmat if layout == "kn" else np.ascontiguousarray(bmat.T), "bf16")
+    ebk = eb if layout == "kn" else np.ascontiguousarray(eb.T)
+    want = ea.astype(np.float64) @ ebk.astype(np.float64)
+    sentinel = np.full(m * ldc * 2, 0x5A, np.uint8)
+    dsts = [dev.upload(sentinel) for _ in range(ndst)]
+    da, db = dev.upload(a), dev.upload(b)
+    desc = gemm_desc(m, n, k, F.BF16, F.BF16, F.B_KN if layout == "kn" else F.B_NK)
+    gemm_multi_store(dev, desc, da.ptr, db.ptr, [d.ptr for d in dsts], ldc, off)
+    dev.sync()
+    bound = gemm_bound(want, np.abs(ea).astype(np.float64) @ np.abs(ebk).astype(np.float64), "bf16", "bf16")
+    for d in dsts:
+        raw = dev.download(d.ptr, m * ldc * 2, np.uint8, (m, ldc * 2))
+        got = from_device_dtype(raw[:, off * 2:(off + n) * 2].copy().view(np.uint16), "bf16")
+        assert np.all(np.abs(got - want) <= bound)
+        assert np.all(raw[:, :off * 2] == 0x5A) and np.all(raw[:, (off + n) * 2:] == 0x5A)
+
+
 def test_multi_store_rejects_misaligned_offsets(dev):
     from tensor_cuda import _ffi as F
     from tensor_cuda.parallel import gemm_multi_store
