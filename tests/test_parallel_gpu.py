@@ -57,13 +57,13 @@ def test_multi_store_writes_every_destination_at_its_offset(dev, dtype_in, dtype
 
 @pytest.mark.parametrize("layout", ["kn", "nk"])
 def test_multi_store_cta_pairs(dev, layout):
-    """A product with at least one 256 x 256 tile per resident CTA pair takes the paired kernel
-    (as the column-split workload's shards do): every destination gets the block, the columns
-    around it stay untouched."""
+    """A single-destination product with at least one 256 x 256 tile per resident CTA pair takes
+    the paired kernel (the column-split workload on one GPU): the block lands at its column
+    offset, the columns around it stay untouched."""
     from tensor_cuda import _ffi as F
     from tensor_cuda.parallel import gemm_multi_store
     from tensor_cuda.runtime import gemm_desc
-    m, n, k, ldc, off, ndst = 2200, 2304, 200, 6912, 2304, 2
+    m, n, k, ldc, off, ndst = 2200, 2304, 200, 6912, 2304, 1
     a, ea = to_device_dtype(O.lcg_gemm(m * k, 5).reshape(m, k), "bf16")
     bmat = O.lcg_gemm(k * n, 6).reshape(k, n)
     b, eb = to_device_dtype(bmat if layout == "kn" else np.ascontiguousarray(bmat.T), "bf16")
