@@ -500,17 +500,17 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
           // consecutive outputs per step, undoing the 128-byte swizzle.
           __syncwarp();
           const int cs = col0 - 32 * half;
-          // The row pointer steps by N per row and the column bounds are fixed for the block; the
-          // loop is unrolled so all 32 rows' stores can be in flight (the GPT-2 LM head: 2.93 ms with
-          // four rows per step and per-row index arithmetic, 2.39 ms like this). Half-word pairs
-          // measured faster than shifted 4-byte stores for rows starting 2 bytes past a 4-byte
-          // boundary (3.96 ms).
+          // The row pointer steps by N per row and the column bounds are fixed for the block; eight
+          // rows per unrolled step (the GPT-2 LM head: 2.93 ms with four rows per step and per-row
+          // index arithmetic, 2.44 ms like this; unrolling all 32 rows gained 2% more but made the
+          // kernel spill). Half-word pairs measured faster than shifted 4-byte stores for rows
+          // starting 2 bytes past a 4-byte boundary (3.96 ms).
           const size_t rb0 = ((size_t)b * p.M + row0) * (size_t)p.N + cs;
           const int rows = p.M - row0 < 32 ? p.M - row0 : 32;
           if (!wide) {
             float *rp = static_cast<float *>(p.c_direct) + rb0;
             const bool colok = cs + lane < p.N;
-#pragma unroll
+#pragma unroll 8
             for (int rr = 0; rr < 32; ++rr, rp += p.N) {
               const uint32_t v = *reinterpret_cast<const uint32_t *>(buf + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4) +
                                                                      ((lane & 3) << 2));
@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
             uint16_t *rp = static_cast<uint16_t *>(p.c_direct) + rb0;
             const int c0 = cs + 2 * lane;
             const bool ok0 = c0 < p.N, ok1 = c0 + 1 < p.N;
-#pragma unroll
+#pragma unroll 8
             for (int rr = 0; rr < 32; ++rr, rp += p.N) {
               const uint32_t v = *reinterpret_cast<const uint32_t *>(buf + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4) +
                                                                      ((lane & 3) << 2));
