@@ -201,29 +201,35 @@ def test_gemm_unaligned_rows_batched(dev, dtype_out, n):
     assert np.array_equal(got, ref.reshape(bsz, m, npad)[:, :, :n].astype(np.float64))
 
 
-@pytest.mark.parametrize("b_layout,dtype_in,dtype_out,epi,n", [
-    ("nk", "bf16", "f32", "", 2200),
-    ("kn", "f16", "f32", "bias+gelu", 2200),
-    ("nk", "bf16", "bf16", "bias+residual", 2200),
-    ("kn", "bf16", "bf16", "", 2201),     # rows not 16-byte aligned: plain stores
+@pytest.mark.parametrize("b_layout,dtype_in,dtype_out,epi,n,m,b_shared", [
+    ("nk", "bf16", "f32", "", 2200, 2200, False),
+    ("kn", "f16", "f32", "bias+gelu", 2200, 2200, False),
+    ("nk", "bf16", "bf16", "bias+residual", 2200, 2200, False),
+    ("kn", "bf16", "bf16", "", 2201, 2200, False),   # rows not 16-byte aligned: plain stores
+    ("nk", "bf16", "bf16", "bias", 2100, 2100, True),  # the odd CTA's last rows and B half past M, N
+    ("kn", "bf16", "f32", "bias+gelu", 2100, 2100, True),
 ])
-def test_gemm_cta_pair_tiles(dev, b_layout, dtype_in, dtype_out, epi, n):
+def test_gemm_cta_pair_tiles(dev, b_layout, dtype_in, dtype_out, epi, n, m, b_shared):
     """Problems with at least one 256 x 256 tile per resident CTA pair run on pairs of SMs (M = 256
-    tensor-core instructions, half of B per SM): batched, with row, column and K tails (M = 2200,
-    K = 200), both B layouts, every epilogue and unaligned output rows, against the oracle."""
+    tensor-core instructions, half of B per SM): batched (B per batch entry or one B broadcast),
+    with row, column and K tails (K = 200; M, N = 2100 leave the odd CTA of the last pair tiles
+    no valid row or column), both B layouts, every epilogue and unaligned output rows, against
+    the oracle."""
     import ctypes as C
     from tensor_cuda import _ffi as F
     from tensor_cuda.runtime import gemm_desc
-    bsz, m, k = 2, 2200, 200
+    bsz, k = 2, 200
     lay = F.B_NK if b_layout == "nk" else F.B_KN
     a_up, a_ex = to_device_dtype(O.lcg_gemm(bsz * m * k, 51).reshape(bsz, m, k), dtype_in)
     b_shape = (n, k) if b_layout == "nk" else (k, n)
-    b_up, b_ex = to_device_dtype(O.lcg_gemm(bsz * n * k, 52).reshape((bsz,) + b_shape), dtype_in)
+    nb = 1 if b_shared else bsz
+    b_up, b_ex = to_device_dtype(O.lcg_gemm(nb * n * k, 52).reshape((nb,) + b_shape), dtype_in)
     bias = O.normal_f32(n, 53, 0, 0.5)
     flags = (F.EPI_BIAS if "bias" in epi else 0) | (F.EPI_GELU if "gelu" in epi else 0)
     eo = F.DTYPE_BYTES[F.DTYPE_CODES[dtype_out]]
     desc = gemm_desc(m, n, k, F.DTYPE_CODES[dtype_in], F.DTYPE_CODES[dtype_out], lay,
-                     flags | (F.EPI_RESIDUAL if "residual" in epi else 0), 1.0, (bsz,), (m * k,), (n * k,))
+                     flags | (F.EPI_RESIDUAL if "residual" in epi else 0), 1.0, (bsz,), (m * k,),
+                     (0 if b_shared else n * k,))
     da, db, dbias = dev.upload(a_up), dev.upload(b_up), dev.upload(bias)
     dc = dev.alloc(bsz * m * n * eo)
     r_ex = None
@@ -238,7 +244,8 @@ def test_gemm_cta_pair_tiles(dev, b_layout, dtype_in, dtype_out, epi, n):
     got = from_device_dtype(dev.download(dc.ptr, bsz * m * n * eo, NP_STORAGE[dtype_out], (bsz * m * n,)),
                             dtype_out).reshape(bsz, m, n).astype(np.float64)
     for i in range(bsz):
-        bt = b_ex[i].T if b_layout == "nk" else b_ex[i]
+        bi = b_ex[0 if b_shared else i]
+        bt = bi.T if b_layout == "nk" else bi
         prod = a_ex[i].astype(np.float64) @ bt.astype(np.float64)
         absprod = np.abs(a_ex[i]).astype(np.float64) @ np.abs(bt).astype(np.float64)
         want = prod
