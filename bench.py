@@ -326,7 +326,7 @@ def run_reference(args, w):
         "impl": "reference", "metric": w["metric"], "value": v, "unit": unit, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": flop_per_step(w) / (v * scale) * 1e3,
         "higher_is_better": True, "scaling": "strong" if w["kind"] == "nsplit" else "weak", "vs_baseline": None,
-        "dtype": "f64 (f32 storage)",
+        "dtype": "f32" if w.get("precision") == "f32" else "f64 (f32 storage)",
         "data": "synthetic", "config": {"workload": args.workload, "description": w["desc"]},
         "cpu_baseline": {"value": v, "unit": unit, "cores": 1 if w["kind"] == "fusion" else threads, "kind": "port",
                          "sample": "per step: " + sample + ("" if w["kind"] == "fusion" else

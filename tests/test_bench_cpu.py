@@ -1,0 +1,36 @@
+"""bench.py's reference arm (the oracle's restatement of the reference's CPU path, timed on the host
+cores) on the CPU: one JSON line with the contract's keys, for a GEMM workload and the fused
+element-wise workload in both evaluation precisions."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def reference_line(*extra):
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "0", "--cpu-seconds", "1", *extra], capture_output=True, text=True, timeout=300,
+                       cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1, r.stdout
+    return json.loads(lines[0])
+
+
+@pytest.mark.parametrize("extra", [("--workload", "batched_gemm_bf16"),
+                                   ("--workload", "fused_elementwise_f32"),
+                                   ("--workload", "fused_elementwise_f32", "--expression", "gelu_chain",
+                                    "--precision", "f32")])
+def test_reference_arm_line(extra):
+    d = reference_line(*extra)
+    assert d["impl"] == "reference" and d["value"] > 0 and d["n_gpus"] == 1
+    assert d["unit"] == d["cpu_baseline"]["unit"] == d["e2e"]["unit"]
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    assert d["config"]["workload"] == extra[1]
+    if "--precision" in extra:
+        assert "gelu" in d["metric"] and "f32 evaluation" in d["metric"] and d["dtype"] == "f32"
