@@ -181,3 +181,23 @@ def test_oracle_f32_rounds_every_node():
     assert f32[:3].tolist() == [0.0, 0.0, 0.0]
     v32 = v.astype(np.float32)
     assert f32[3] == (v32[3] + np.float32(1e-8)) - v32[3]
+
+
+def test_oracle_f32_mode_is_ieee_f32_arithmetic():
+    """The oracle's f32 evaluation (every node rounded to f32) equals NumPy's float32 arithmetic
+    step by step for +, -, *, / and sqrt, which is what the device's f32 mode is held to bit for
+    bit; transcendental nodes are the correctly rounded f32 of the f64 value."""
+    rng = np.random.default_rng(31)
+    a, b, c = (rng.standard_normal(20000).astype(np.float32) * 3 for _ in range(3))
+    x, y, z = Traced.input(0), Traced.input(1), Traced.input(2)
+    e = x.add(y).mul(z).sub(x).div(y.add(3.5)).max(x.mul(0.1)).add(z.mul(z).mul(1.0 / 3.0)).abs().sqrt()
+    got = O.eval_ir(e.node, [a, b, c], precision="f32")
+    f = np.float32
+    with np.errstate(all="ignore"):
+        t = ((a + b) * c - a) / (b + f(3.5))
+        t = np.where(t >= a * f(0.1), t, a * f(0.1))
+        want = np.sqrt(np.abs(t + (c * c) * f(1.0 / 3.0)))
+    assert want.dtype == np.float32
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    ex = O.eval_ir(x.exp().node, [a], precision="f32")
+    assert np.array_equal(ex, np.exp(a.astype(np.float64)).astype(np.float32))
