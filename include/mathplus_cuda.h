@@ -149,17 +149,26 @@ int mpc_gemm_residual(mpc_device *dev, const mpc_gemm_desc *desc, const void *A,
                       const float *bias, const void *R, mpc_stream s);
 
 /* Allocation-free variant of the f32 (3xTF32) path of mpc_gemm. It has no counterpart in the
- * reference: it exists for callers that cannot allocate device memory (code running during
- * CUDA-graph capture, runtimes that own every device byte or hand out a fixed budget). Its
- * scratch (the tf32 hi/lo planes, and a padded copy of C when C's rows are not 16-byte aligned)
- * lives in one static device array of 32 MiB that every GPU loading the library holds until
- * exit; requests needing more return MPC_ERR_INVALID. It uses the calling thread's current
- * device and the given stream (NULL = the legacy default stream) and needs no mpc_device. The
- * first call on a device resolves the array's address (cudaGetSymbolAddress): make it before any
- * stream capture. All calls share the array: calls that overlap on the GPU race. desc must say
- * f32 in and out; everything else is as for mpc_gemm. */
+ * reference: it exists for callers that cannot allocate device memory (a host runtime that owns
+ * every device byte, or hands this library a fixed budget it may not grow). Its scratch (the tf32
+ * hi/lo planes, and a padded copy of C when C's rows are not 16-byte aligned) lives in one static
+ * device array of 32 MiB that every GPU loading the library holds until exit; requests needing more
+ * return MPC_ERR_INVALID. It uses the calling thread's current device and the given stream (NULL =
+ * the legacy default stream) and needs no mpc_device. The first call on a device resolves the
+ * array's address (cudaGetSymbolAddress): make it before any stream capture; that set-up is not
+ * redone after cudaDeviceReset. All calls share the array: calls that overlap on the GPU race.
+ * desc must say f32 in and out; everything else is as for mpc_gemm. A kernel wait that runs out is
+ * not reported by the call itself (it returns before the kernels run): see
+ * mpc_gemm_f32_noalloc_status. */
 int mpc_gemm_f32_noalloc(const mpc_gemm_desc *desc, const float *A, const float *B, float *C,
                          const float *bias, mpc_stream s);
+/* Waits for stream s, then reports whether a bounded wait inside any mpc_gemm_f32_noalloc kernel on
+ * the current device ran out since the last query (MPC_ERR_TIMEOUT: that call's C is incomplete) and
+ * clears the record. Allocates nothing. */
+int mpc_gemm_f32_noalloc_status(mpc_stream s);
+/* Failure-path self test of that record: one wait on an mbarrier nothing releases, limited to
+ * timeout_ns, recorded where mpc_gemm_f32_noalloc's kernels record theirs (no fault, trap or hang). */
+int mpc_gemm_f32_noalloc_selftest(uint64_t timeout_ns, mpc_stream s);
 
 /* ---- fused scaled-dot-product attention ----------------------------------------------------
  * softmax(scale * Q·Kᵀ + mask) · V over Q [B,H,Lq,D], K [B,Hk,Lk,D], V [B,Hk,Lk,Dv] into
@@ -321,9 +330,19 @@ int mpc_fused_lower(const int32_t *code, int32_t n_instr, const double *consts, 
                     const int32_t *dtypes, uint32_t flags, int32_t check_compile, char *buf, size_t cap,
                     size_t *len);
 
-/* ---- multi-GPU: NCCL over NVLink, one rank per process (no reference counterpart) ---------- */
+/* ---- multi-GPU: NCCL over NVLink, one rank per process (no reference counterpart) ----------
+ * Communicators are created non-blocking and every NCCL call on one is waited for with a deadline,
+ * so a rank that never joins (or never reaches a collective) cannot hold the others forever: the
+ * call returns MPC_ERR_TIMEOUT instead (the graceful, never-hang contract the reference's native
+ * loader keeps, packages/tensor-wasm/src/native.ts:128-139). */
 int mpc_comm_unique_id(void *id128);
+/* mpc_comm_init_timeout with a 10-minute limit. */
 int mpc_comm_init(mpc_device *dev, int nranks, int rank, const void *id128, mpc_comm **comm);
+/* Joins rank `rank` of `nranks` to the communicator named by id128. When the group is not complete
+ * within timeout_ms (a rank that never calls init), the half-built communicator is aborted and the
+ * call returns MPC_ERR_TIMEOUT; later NCCL calls on the communicator use the same limit. */
+int mpc_comm_init_timeout(mpc_device *dev, int nranks, int rank, const void *id128, int64_t timeout_ms,
+                          mpc_comm **comm);
 int mpc_comm_destroy(mpc_comm *comm);
 int mpc_comm_abort(mpc_comm *comm);
 /* Gathers `bytes` from every rank into recv (rank r's block at offset r*bytes). */

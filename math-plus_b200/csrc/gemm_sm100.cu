@@ -950,22 +950,23 @@ int gemm_run_multi(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const
 // ---------------------------------------------------------------------------------------------
 // Allocation-free f32 GEMM (3xTF32) for callers that cannot allocate device memory.
 //
-// Some callers of this library may not call cudaMalloc: code running while a CUDA graph is being
-// captured, a host runtime that hands the library a fixed, pre-sized memory budget, or a caller
-// whose own allocator owns every device byte. mpc_gemm's f32 path needs scratch memory for the
-// tf32 hi / lo planes of A and B (and a pitch-padded copy of C when C's rows are not 16-byte
-// aligned), which it takes from the device allocator. mpc_gemm_f32_noalloc runs the same kernels
-// with that scratch in one file-scope device array instead: it allocates nothing and needs no
-// mpc_device handle, working on the calling thread's current CUDA device and the given stream.
+// Some callers of this library may not call cudaMalloc: a host runtime that hands the library a
+// fixed, pre-sized memory budget, or a caller whose own allocator owns every device byte.
+// mpc_gemm's f32 path needs scratch memory for the tf32 hi / lo planes of A and B (and a
+// pitch-padded copy of C when C's rows are not 16-byte aligned), which it takes from the device
+// allocator. mpc_gemm_f32_noalloc runs the same kernels with that scratch in one file-scope device
+// array instead: it allocates nothing and needs no mpc_device handle, working on the calling
+// thread's current CUDA device and the given stream.
 //
 // The array is kNoAllocScratchBytes (32 MiB) plus a 256-byte header holding the kernels' error
 // word. Every GPU that loads this library holds it until the process exits. All calls share it
-// and it keeps the last call's contents: each call clears the error word and rewrites every
-// scratch byte it reads, but two calls whose work overlaps on the GPU (different streams, or
-// devices sharing nothing but the host thread are fine) race on the array; serialise them.
-// The first call on a device sets up that device (it resolves the array's device address with
-// cudaGetSymbolAddress and reads the device properties); make that first call before any stream
-// capture. A kernel-side wait timeout is recorded in the error word but not reported here.
+// and it keeps the last call's contents: each call rewrites every scratch byte it reads, but two
+// calls whose work overlaps on the GPU (different streams, or no ordering between them) race on the
+// array; serialise them. The first call on a device sets up that device (it resolves the array's
+// device address with cudaGetSymbolAddress and reads the device properties); make that first call
+// before any stream capture. The set-up is not redone after cudaDeviceReset. A kernel-side wait that
+// runs out leaves its site in the error word, which later calls keep (no call clears it):
+// mpc_gemm_f32_noalloc_status reads it and clears it.
 // ---------------------------------------------------------------------------------------------
 namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
@@ -979,17 +980,13 @@ struct NoAllocDevice {
   mpc_device lite;                // ordinal, properties and error word for the shared launch code
 };
 NoAllocDevice g_noalloc[64];
-}  // namespace
-}  // namespace mpc
 
-extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, const float *B, float *Cout,
-                                    const float *bias, mpc_stream s) {
-  using namespace mpc;
-  using namespace mpc::gemm;
+// The calling thread's current device, set up once (see above).
+int noalloc_device(const char *who, NoAllocDevice **out) {
   int ord = -1;
   cudaError_t e = cudaGetDevice(&ord);
-  if (e != cudaSuccess) return cuda_fail(nullptr, e, "mpc_gemm_f32_noalloc: cudaGetDevice");
-  if (ord < 0 || ord >= 64) return fail(MPC_ERR_UNSUPPORTED, "mpc_gemm_f32_noalloc: device ordinal %d", ord);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, who);
+  if (ord < 0 || ord >= 64) return fail(MPC_ERR_UNSUPPORTED, "%s: device ordinal %d", who, ord);
   NoAllocDevice &nd = g_noalloc[ord];
   std::call_once(nd.once, [&] {
     void *p = nullptr;
@@ -1003,100 +1000,102 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
     nd.lite.ordinal = ord;
     nd.lite.d_err = reinterpret_cast<int *>(nd.base);
   });
-  if (nd.status != MPC_OK) return fail(nd.status, "mpc_gemm_f32_noalloc: set-up of device %d failed earlier", ord);
-  if (!d) return fail(MPC_ERR_INVALID, "mpc_gemm_f32_noalloc: null descriptor");
+  if (nd.status != MPC_OK) return fail(nd.status, "%s: set-up of device %d failed earlier", who, ord);
+  *out = &nd;
+  return MPC_OK;
+}
+}  // namespace
+}  // namespace mpc
+
+extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, const float *B, float *Cout,
+                                    const float *bias, mpc_stream s) {
+  using namespace mpc;
+  using namespace mpc::gemm;
+  const char *who = "mpc_gemm_f32_noalloc";
+  NoAllocDevice *nd = nullptr;
+  int rc = noalloc_device(who, &nd);
+  if (rc) return rc;
+  if (!d) return fail(MPC_ERR_INVALID, "%s: null descriptor", who);
   if (d->dtype_in != MPC_F32 || d->dtype_out != MPC_F32)
-    return fail(MPC_ERR_INVALID, "mpc_gemm_f32_noalloc: f32 inputs and output only (got %d -> %d)", d->dtype_in,
-                d->dtype_out);
-  const int64_t M = d->m, N = d->n, K = d->k;
-  if (M < 0 || N < 0 || K < 0) return fail(MPC_ERR_INVALID, "mpc_gemm_f32_noalloc: negative dimension");
-  if (d->b_layout != MPC_B_KN && d->b_layout != MPC_B_NK)
-    return fail(MPC_ERR_INVALID, "mpc_gemm_f32_noalloc: b_layout %d", d->b_layout);
-  if (d->batch_rank < 0 || d->batch_rank > 4)
-    return fail(MPC_ERR_INVALID, "mpc_gemm_f32_noalloc: batch_rank %d", d->batch_rank);
-  if ((d->epilogue & MPC_EPI_BIAS) && !bias) return fail(MPC_ERR_INVALID, "mpc_gemm_f32_noalloc: BIAS without bias");
-  Params p{};
-  int64_t batch = 1, nA = 1, nB = 1;
-  p.brank = d->batch_rank;
-  for (int i = 0; i < d->batch_rank; ++i) {
-    const int64_t sz = d->batch_shape[i], sa = d->a_batch_stride[i], sb = d->b_batch_stride[i];
-    if (sz < 0 || sa < 0 || sb < 0 || (M * K && sa % (M * K)) || (K * N && sb % (K * N)))
-      return fail(MPC_ERR_INVALID, "mpc_gemm_f32_noalloc: batch axis %d (shape %lld, strides %lld, %lld)", i,
-                  (long long)sz, (long long)sa, (long long)sb);
-    batch *= sz;
-    p.bshape[i] = (int)sz;
-    p.a_bstride[i] = M * K ? (int)(sa / (M * K)) : 0;
-    p.b_bstride[i] = K * N ? (int)(sb / (K * N)) : 0;
-    if (sz > 0) {
-      nA += (sz - 1) * p.a_bstride[i];
-      nB += (sz - 1) * p.b_bstride[i];
-    }
-  }
+    return fail(MPC_ERR_INVALID, "%s: f32 inputs and output only (got %d -> %d)", who, d->dtype_in, d->dtype_out);
+  if (d->epilogue & MPC_EPI_RESIDUAL) return fail(MPC_ERR_UNSUPPORTED, "%s: no RESIDUAL epilogue", who);
+  mpc_device *dev = &nd->lite;
+  Params p;
+  Prep pr;
+  // The same validation and kernel choice as mpc_gemm's f32 path (tile limits, the 128 x 64 tiles
+  // for problems with fewer 128 x 128 tiles than SMs).
+  if ((rc = prepare(dev, d, bias, who, p, pr))) return rc;
+  const int64_t M = d->m, N = d->n, K = d->k, batch = pr.batch;
   if (batch == 0 || M == 0 || N == 0) return MPC_OK;
-  if (!A || !B || !Cout) return fail(MPC_ERR_INVALID, "mpc_gemm_f32_noalloc: null operand pointer");
+  if (!A || !B || !Cout) return fail(MPC_ERR_INVALID, "%s: null operand pointer", who);
   // Scratch layout: A_hi | A_lo | B_hi | B_lo (K pitch rounded to 4 floats), then C staging.
   const int64_t ldk = round_up(K, 4);
   const bool stage_c = ((uintptr_t)Cout & 15) || (N % 4);
   const int64_t ldc = stage_c ? round_up(N, 4) : N;
-  const size_t a_plane = (size_t)(nA * M * ldk) * 4, b_plane = (size_t)(nB * N * ldk) * 4;
+  const size_t a_plane = (size_t)(pr.nA * M * ldk) * 4, b_plane = (size_t)(pr.nB * N * ldk) * 4;
   const size_t need = 2 * a_plane + 2 * b_plane + (stage_c ? (size_t)(batch * M * ldc) * 4 : 0);
   if (K > 0 && need > kNoAllocScratchBytes)
     return fail(MPC_ERR_INVALID,
-                "mpc_gemm_f32_noalloc: needs %zu bytes of scratch, above its %zu-byte static maximum "
-                "(use mpc_gemm for this size)",
+                "%s: needs %zu bytes of scratch, above its %zu-byte static maximum (use mpc_gemm for this size)", who,
                 need, kNoAllocScratchBytes);
   cudaStream_t st = static_cast<cudaStream_t>(s);
-  mpc_device *dev = &nd.lite;
-  MPC_CUDA(dev, cudaMemsetAsync(dev->d_err, 0, sizeof(int), st));  // the shared error word starts clear
   if (K == 0) {
     fill_epilogue_kernel<<<1184, 256, 0, st>>>(Cout, MPC_F32, batch * M, N, bias, d->epilogue);
     return check_launch(dev, "fill_epilogue_kernel");
   }
-  unsigned char *scratch = nd.base + kNoAllocHeader;
+  unsigned char *scratch = nd->base + kNoAllocHeader;
   float *a_hi = reinterpret_cast<float *>(scratch), *a_lo = reinterpret_cast<float *>(scratch + a_plane);
   float *b_hi = reinterpret_cast<float *>(scratch + 2 * a_plane);
   float *b_lo = reinterpret_cast<float *>(scratch + 2 * a_plane + b_plane);
   float *cdst = stage_c ? reinterpret_cast<float *>(scratch + 2 * a_plane + 2 * b_plane) : Cout;
-  if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return fail(MPC_ERR_UNSUPPORTED, "dimension above 2^30");
-  p.M = (int)M;
-  p.N = (int)N;
-  p.K = (int)K;
-  p.tiles_m = (int)((M + 127) / 128);
-  p.tiles_n = (int)((N + 127) / 128);
-  p.tiles_total = (int)(batch * p.tiles_m * p.tiles_n);
-  p.k_blocks = (int)((K + 31) / 32);
-  p.group_m = 16;
-  p.alpha = d->alpha;
-  p.bias = bias;
-  if (d->epilogue & MPC_EPI_RESIDUAL)
-    return fail(MPC_ERR_UNSUPPORTED, "mpc_gemm_f32_noalloc: no RESIDUAL epilogue");
-  p.epilogue = d->epilogue & (MPC_EPI_BIAS | MPC_EPI_GELU);
-  p.idesc = make_idesc(kFmtTF32, false, 128, 128);
-  p.out_dtype = MPC_F32;
-  p.err = dev->d_err;
-  p.timeout_ns = dev->timeout_ns;
-  p.ndst = 1;
-  split_rows_kernel<<<1184, 256, 0, st>>>(A, a_hi, a_lo, nA * M, K, ldk);
+  split_rows_kernel<<<1184, 256, 0, st>>>(A, a_hi, a_lo, pr.nA * M, K, ldk);
   if (d->b_layout == MPC_B_NK) {
-    split_rows_kernel<<<1184, 256, 0, st>>>(B, b_hi, b_lo, nB * N, K, ldk);
+    split_rows_kernel<<<1184, 256, 0, st>>>(B, b_hi, b_lo, pr.nB * N, K, ldk);
   } else {
-    dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)nB);
+    dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)pr.nB);
     split_transpose_kernel<<<g, dim3(32, 8), 0, st>>>(B, b_hi, b_lo, (int)K, (int)N, (int)ldk);
   }
-  int rc = check_launch(dev, "split_tf32");
-  if (rc) return rc;
+  if ((rc = check_launch(dev, "split_tf32"))) return rc;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
   const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   const CUtensorMapSwizzle SW = CU_TENSOR_MAP_SWIZZLE_128B;
-  if ((rc = make_map_3d(&maps.a, f32, a_hi, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
-      (rc = make_map_3d(&maps.a_lo, f32, a_lo, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
-      (rc = make_map_3d(&maps.b, f32, b_hi, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)) ||
-      (rc = make_map_3d(&maps.b_lo, f32, b_lo, K, N, nB, ldk * 4, N * ldk * 4, 32, 128, SW)) ||
+  if ((rc = make_map_3d(&maps.a, f32, a_hi, K, M, pr.nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
+      (rc = make_map_3d(&maps.a_lo, f32, a_lo, K, M, pr.nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
+      (rc = make_map_3d(&maps.b, f32, b_hi, K, N, pr.nB, ldk * 4, N * ldk * 4, 32, pr.BN, SW)) ||
+      (rc = make_map_3d(&maps.b_lo, f32, b_lo, K, N, pr.nB, ldk * 4, N * ldk * 4, 32, pr.BN, SW)) ||
       (rc = make_map_3d(&maps.c[0], f32, cdst, N, M, batch, ldc * 4, M * ldc * 4, 32, 32, SW)))
     return rc;
-  if ((rc = launch<kTF32x3, false, 128, 3>(dev, maps, p, st))) return rc;
+  rc = pr.BN == 64 ? launch<kTF32x3, false, 64, 4>(dev, maps, p, st) : launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
+  if (rc) return rc;
   if (stage_c)
     MPC_CUDA(dev, cudaMemcpy2DAsync(Cout, N * 4, cdst, ldc * 4, N * 4, batch * M, cudaMemcpyDeviceToDevice, st));
   return MPC_OK;
+}
+
+extern "C" int mpc_gemm_f32_noalloc_status(mpc_stream s) {
+  using namespace mpc;
+  const char *who = "mpc_gemm_f32_noalloc_status";
+  NoAllocDevice *nd = nullptr;
+  int rc = noalloc_device(who, &nd);
+  if (rc) return rc;
+  MPC_CUDA(nullptr, cudaStreamSynchronize(static_cast<cudaStream_t>(s)));
+  int word = 0;
+  MPC_CUDA(nullptr, cudaMemcpy(&word, nd->lite.d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (word == 0) return MPC_OK;
+  MPC_CUDA(nullptr, cudaMemset(nd->lite.d_err, 0, sizeof(int)));
+  return fail(MPC_ERR_TIMEOUT,
+              "%s: a kernel's bounded wait (site 0x%x) ran out in an earlier mpc_gemm_f32_noalloc call on device %d; "
+              "that call's output is incomplete",
+              who, word, nd->lite.ordinal);
+}
+
+extern "C" int mpc_gemm_f32_noalloc_selftest(uint64_t timeout_ns, mpc_stream s) {
+  using namespace mpc;
+  const char *who = "mpc_gemm_f32_noalloc_selftest";
+  if (timeout_ns == 0 || timeout_ns > 10000000000ull) return fail(MPC_ERR_INVALID, "%s: timeout must be in (0, 10 s]", who);
+  NoAllocDevice *nd = nullptr;
+  int rc = noalloc_device(who, &nd);
+  if (rc) return rc;
+  return wait_probe_run(&nd->lite, timeout_ns, static_cast<cudaStream_t>(s));
 }

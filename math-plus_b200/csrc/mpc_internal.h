@@ -51,8 +51,9 @@ struct mpc_device {
 // One rank of an NCCL communicator (comm.cu).
 struct mpc_comm {
   mpc_device *dev;
-  void *comm;  // ncclComm_t
+  void *comm;  // ncclComm_t (non-blocking)
   int nranks, rank;
+  int64_t timeout_ms;  // limit for each NCCL call on it to settle
 };
 
 namespace mpc {

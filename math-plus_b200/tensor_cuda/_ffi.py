@@ -128,6 +128,8 @@ SIGNATURES = {
     "mpc_mean_pool": [_dev, _vp, _i32, _vp, _i32, _vp, _i64, _i64, _i64, _vp],
     "mpc_gemm_residual": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp, _vp],
     "mpc_gemm_f32_noalloc": [C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
+    "mpc_gemm_f32_noalloc_status": [_vp],
+    "mpc_gemm_f32_noalloc_selftest": [_u64, _vp],
     "mpc_sdpa": [_dev, C.POINTER(SdpaDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp],
     "mpc_softmax": [_dev, _vp, _i32, _vp, _i64, _i64, _i64, _vp],
     "mpc_gelu": [_dev, _vp, _i32, _vp, _i32, _i64, _vp],
@@ -138,6 +140,7 @@ SIGNATURES = {
     "mpc_transpose": [_dev, _vp, _vp, _i32, _i32, C.POINTER(_i64), C.POINTER(_i32), _vp],
     "mpc_comm_unique_id": [_vp],
     "mpc_comm_init": [_dev, C.c_int, C.c_int, _vp, C.POINTER(_vp)],
+    "mpc_comm_init_timeout": [_dev, C.c_int, C.c_int, _vp, _i64, C.POINTER(_vp)],
     "mpc_comm_destroy": [_vp],
     "mpc_comm_abort": [_vp],
     "mpc_allgather": [_vp, _vp, _vp, _sz, _vp],

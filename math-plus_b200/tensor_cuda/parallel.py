@@ -35,12 +35,19 @@ class PeerGroup:
     """One rank of a communicator (``mpc_comm``). Collective calls must be made by every rank in
     the same order."""
 
-    def __init__(self, device: Device, rank: int, world: int, uid: bytes):
+    def __init__(self, device: Device, rank: int, world: int, uid: bytes, timeout_ms: int | None = None):
+        """Joins the group; with ``timeout_ms``, a group that is not complete in time (a rank that
+        never joins) raises ``MpcError`` with status TIMEOUT instead of waiting (the default limit
+        is 10 minutes)."""
         if len(uid) != 128:
             raise ValueError("PeerGroup: the id is 128 bytes (from unique_id() on one rank)")
         self.device, self.rank, self.world = device, rank, world
         h = C.c_void_p()
-        F.call("mpc_comm_init", device.handle, world, rank, (C.c_uint8 * 128).from_buffer_copy(uid), C.byref(h))
+        uid_buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        if timeout_ms is None:
+            F.call("mpc_comm_init", device.handle, world, rank, uid_buf, C.byref(h))
+        else:
+            F.call("mpc_comm_init_timeout", device.handle, world, rank, uid_buf, int(timeout_ms), C.byref(h))
         self.handle = h.value
 
     @classmethod

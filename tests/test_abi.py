@@ -88,6 +88,7 @@ def test_calls_fail_with_status_not_abort(lib):
     assert "null device" in F.last_error()
     assert lib.mpc_device_count(None) == F.ERR_INVALID
     assert lib.mpc_comm_init(None, 2, 0, None, None) == F.ERR_INVALID
+    assert lib.mpc_comm_init_timeout(None, 2, 0, None, C.c_int64(1000), None) == F.ERR_INVALID
 
 
 def test_missing_library_raises_instead_of_falling_back(tmp_path):

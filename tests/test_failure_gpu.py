@@ -6,6 +6,9 @@
   mpc_device_clear_error, and the same context then runs a GEMM correctly (the wasm backend's
   trap-poisoning rule, packages/tensor-wasm/src/index.ts:291-340, with an explicit reset);
 * invalid shapes and strides rejected before any launch;
+* a rank that never joins the communicator (one GPU; rank 1 is a process that never calls init):
+  rank 0's init gives up after its limit with MPC_ERR_TIMEOUT, the half-built communicator is
+  aborted on the host, and the device stays usable;
 * two ranks (skipped on one GPU): one rank never enters a peer barrier; the other's barrier
   kernel gives up after the short wait limit and its next synchronisation reports MPC_ERR_TIMEOUT.
 """
@@ -83,6 +86,16 @@ def test_invalid_shapes_and_strides_are_rejected_before_launch(dev):
         F.call("mpc_transpose", dev.handle, C.c_void_p(buf.ptr), C.c_void_p(buf.ptr), 4, 2, shape, perm, None)
     assert dev.launch_count() == before
     assert dev.status() == F.OK
+
+
+def test_a_rank_that_never_joins_the_communicator_times_out():
+    """Runs in a child process with its own time limit, NVLS off."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=os.pathsep.join(
+        [ROOT, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "math-plus_b200"), os.path.join(ROOT, "tests")]))
+    cmd = ["timeout", "-k", "20", "180", sys.executable, os.path.join(ROOT, "tests", "_comm_init_timeout.py")]
+    r = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    assert "rank 0 timed out as expected" in r.stdout and "device usable" in r.stdout
 
 
 def _gpu_count():
