@@ -148,6 +148,24 @@ int mpc_gemm(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const vo
 int mpc_gemm_residual(mpc_device *dev, const mpc_gemm_desc *desc, const void *A, const void *B, void *C,
                       const float *bias, const void *R, mpc_stream s);
 
+/* What the GEMM and attention kernels use on a device (gemmCapabilities,
+ * packages/tensor-webgpu/src/gemm-caps.ts:60-86: the record of optional features a device's GEMM
+ * may use). Advisory: every call still runs on the device whatever the record says. */
+typedef struct {
+  int32_t f16;                    /* f16 operands, f32 accumulation (tcgen05.mma kind::f16) */
+  int32_t bf16;                   /* bf16 operands, f32 accumulation */
+  int32_t f32_3xtf32;             /* f32 operands as 3xTF32 (kind::tf32 on hi / lo parts) */
+  int32_t cta_pairs;              /* 256 x 256 output tiles on the two SMs of a TPC (cta_group::2) */
+  int32_t sm_count;
+  int32_t pair_min_tiles;         /* f16 / bf16 problems with at least this many 256 x 256 tiles run on pairs */
+  int32_t tf32_narrow_below;      /* f32 problems with fewer 128 x 128 tiles than this run 128 x 64 tiles */
+  int32_t attention_tc_head_dims; /* bit mask of head dims on the tensor-core attention path: 1 = 64, 2 = 128 */
+  int32_t attention_max_head_dim; /* largest head dim of the CUDA-core attention path */
+  int32_t reserved;
+  int64_t max_dim;                /* largest M, N, K (and attention L) */
+} mpc_gemm_caps;
+int mpc_gemm_capabilities(mpc_device *dev, mpc_gemm_caps *caps);
+
 /* Allocation-free variant of the f32 (3xTF32) path of mpc_gemm. It has no counterpart in the
  * reference: it exists for callers that cannot allocate device memory (a host runtime that owns
  * every device byte, or hands this library a fixed budget it may not grow). Its scratch (the tf32

@@ -900,6 +900,20 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
   return rc;
 }
 
+int gemm_capabilities(mpc_device *dev, mpc_gemm_caps *c) {
+  memset(c, 0, sizeof(*c));
+  // The conditions prepare() applies when it picks a kernel, reported rather than re-derived.
+  c->f16 = c->bf16 = c->f32_3xtf32 = 1;
+  c->cta_pairs = dev->prop.major == 10 ? 1 : 0;
+  c->sm_count = dev->prop.multiProcessorCount;
+  c->pair_min_tiles = dev->prop.multiProcessorCount / 2;
+  c->tf32_narrow_below = dev->prop.multiProcessorCount;
+  c->attention_tc_head_dims = 1 | 2;
+  c->attention_max_head_dim = 256;
+  c->max_dim = int64_t(1) << 30;
+  return MPC_OK;
+}
+
 // The product stored into several row-major matrices at once (row pitch ldc elements, columns
 // col_offset .. col_offset + N - 1 of each): the epilogue issues one TMA store per destination for
 // every output block. With the destinations being every rank's copy of a column-split result in

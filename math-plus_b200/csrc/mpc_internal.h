@@ -131,6 +131,7 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
 int sdpa_run(mpc_device *dev, const mpc_sdpa_desc *d, const void *Q, const void *K, const void *V, const void *mask,
              void *O, float *LSE, const mpc_sdpa_layout *layout, cudaStream_t st);
 int wait_probe_run(mpc_device *dev, uint64_t timeout_ns, cudaStream_t st);
+int gemm_capabilities(mpc_device *dev, mpc_gemm_caps *caps);
 // The product stored into `ndst` row-major matrices (pitch ldc, columns col_offset..+N-1).
 int gemm_run_multi(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void *B, const float *bias,
                    void *const *dsts, int ndst, int64_t ldc, int64_t col_offset, cudaStream_t st);

@@ -301,6 +301,11 @@ int mpc_device_info(mpc_device *dev, mpc_device_info_t *info) {
   return MPC_OK;
 }
 
+int mpc_gemm_capabilities(mpc_device *dev, mpc_gemm_caps *caps) {
+  if (!dev || !caps) return fail(MPC_ERR_INVALID, "mpc_gemm_capabilities: null argument");
+  return gemm_capabilities(dev, caps);
+}
+
 int mpc_device_status(mpc_device *dev) {
   if (!dev) return fail(MPC_ERR_INVALID, "null device handle");
   return dev->sticky;

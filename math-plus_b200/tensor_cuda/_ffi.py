@@ -127,6 +127,7 @@ SIGNATURES = {
     "mpc_geglu": [_dev, _vp, _i32, _vp, _i64, _i64, _vp],
     "mpc_mean_pool": [_dev, _vp, _i32, _vp, _i32, _vp, _i64, _i64, _i64, _vp],
     "mpc_gemm_residual": [_dev, C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp, _vp],
+    "mpc_gemm_capabilities": [_dev, _vp],
     "mpc_gemm_f32_noalloc": [C.POINTER(GemmDesc), _vp, _vp, _vp, _vp, _vp],
     "mpc_gemm_f32_noalloc_status": [_vp],
     "mpc_gemm_f32_noalloc_selftest": [_u64, _vp],

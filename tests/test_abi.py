@@ -54,6 +54,7 @@ int main(void) {
          offsetof(mpc_gemm_desc, batch_shape), offsetof(mpc_gemm_desc, b_batch_stride), sizeof(mpc_sdpa_desc));
   printf("%zu %zu %zu\n", offsetof(mpc_sdpa_desc, scale), offsetof(mpc_sdpa_desc, mask_strides),
          sizeof(mpc_device_info_t));
+  printf("%zu %zu\n", sizeof(mpc_gemm_caps), offsetof(mpc_gemm_caps, max_dim));
   return 0;
 }
 '''
@@ -72,6 +73,9 @@ int main(void) {
     assert vals[5] == F.SdpaDesc.scale.offset
     assert vals[6] == F.SdpaDesc.mask_strides.offset
     assert vals[7] == C.sizeof(F.DeviceInfo)
+    from tensor_cuda.caps import GemmCapsStruct
+    assert vals[8] == C.sizeof(GemmCapsStruct)
+    assert vals[9] == GemmCapsStruct.max_dim.offset
 
 
 def test_calls_fail_with_status_not_abort(lib):
@@ -89,6 +93,7 @@ def test_calls_fail_with_status_not_abort(lib):
     assert lib.mpc_device_count(None) == F.ERR_INVALID
     assert lib.mpc_comm_init(None, 2, 0, None, None) == F.ERR_INVALID
     assert lib.mpc_comm_init_timeout(None, 2, 0, None, C.c_int64(1000), None) == F.ERR_INVALID
+    assert lib.mpc_gemm_capabilities(None, None) == F.ERR_INVALID
 
 
 def test_missing_library_raises_instead_of_falling_back(tmp_path):

@@ -232,3 +232,16 @@ def test_elementwise_reduction_and_scalar_operands(dev):
         a.logicalNot()
     with pytest.raises(TypeError, match="not defined for bool"):
         gt.sum()
+
+
+def test_gemm_capabilities_record():
+    """gemmCapabilities (packages/tensor-webgpu/src/gemm-caps.ts:60-86): what the GEMM and attention
+    use on this device."""
+    from tensor_cuda.caps import gemm_capabilities
+    from tensor_cuda.device import create_cuda_device
+    cdev = create_cuda_device(0)
+    caps = gemm_capabilities(cdev)
+    assert caps.f16 and caps.bf16 and caps.f32_3xtf32 and caps.cta_pairs
+    assert caps.sm_count == cdev.info["sm_count"] and caps.pair_min_tiles == caps.sm_count // 2
+    assert caps.attention_head_dims == (64, 128) and caps.attention_max_head_dim == 256
+    assert caps.max_dim == 1 << 30
