@@ -27,6 +27,10 @@ A step is one pass of the hot path over one batch of synthetic input:
                                packages/tensor-webgpu/test/fusion.test.ts:157-163); GB/s of the
                                16 bytes each element reads and writes.
 
+The default run (batched_gemm_bf16) also times causal_attention_f16 and reports it under
+"secondary" in the same line (the metric's fused-attention half); --no-secondary skips it.
+--threshold-sweep measures the host-array GEMM crossover behind tensor_cuda.caps.choose_gemm_backend.
+
 ``value`` is device-timed throughput with inputs resident in HBM (CUDA events on the launching
 stream, barrier + synchronize around the timed region, max over ranks). ``e2e`` runs the same
 step through the C ABI from pinned HOST buffers: the host->device copies of the inputs and the
@@ -84,6 +88,10 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true",
+                    help="time only --workload (the default run also times the causal attention configuration)")
+    ap.add_argument("--threshold-sweep", action="store_true",
+                    help="measure the host-array GEMM crossover (device end to end vs one CPU thread) and exit")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work for the baseline sample")
     ap.add_argument("--batch", type=int, default=None, help="override the per-rank batch (small profiling cases)")
     ap.add_argument("--elements", type=int, default=None,
@@ -309,31 +317,110 @@ def cpu_sample_rate(w: dict, target_s: float, threads: int):
                              else ", f64 accumulate"), t
 
 
-def run_reference(args, w):
-    world, rank, _ = dist_env()
-    if rank != 0:
-        return
-    threads = len(os.sched_getaffinity(0))
-    rates, sample = [], ""
+# ---------------------------------------------------------------------------------------------
+# The host-array GEMM crossover (chooseGemmBackend, packages/tensor-webgpu/src/threshold.ts:67-85)
+# ---------------------------------------------------------------------------------------------
+
+THRESHOLD_SHAPES = ([(n, n, n) for n in (8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 256, 384, 512)] +
+                    [(mn, kk, mn) for mn in (32, 64, 128, 256) for kk in (16, 64, 256, 1024, 4096)] +
+                    [(16, 1024, 3072), (1, 768, 50257)])
+
+
+def run_threshold_sweep(args):
+    """Per (m, k, n): the device end to end from host f32 arrays (pageable A and B copied up, the f32
+    GEMM, C copied back, wall clock, median) against the reference's CPU algorithm (the oracle's
+    restatement of tensor-core gemmNT, one host thread). Prints one JSON line with every shape and
+    the (m·n, m·n·k) thresholds that send the most shapes to the device without sending any that
+    measured slower there."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from tensor_cuda import _ffi as F
+    from tensor_cuda.runtime import Device, gemm_desc
+    dev = Device.shared(0)
+    rng = np.random.default_rng(11)
+    rows = []
+
+    def timed(fn, budget_s):
+        fn()
+        ts = []
+        t_end = time.perf_counter() + budget_s
+        while len(ts) < 5 or (time.perf_counter() < t_end and len(ts) < 200):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    for m, k, n in THRESHOLD_SHAPES:
+        a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+        b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+        c = np.empty((m, n), np.float32)
+        desc = gemm_desc(m, n, k, F.F32, F.F32, F.B_KN)
+
+        def device_call():
+            da, db, dc = dev.alloc(a.nbytes), dev.alloc(b.nbytes), dev.alloc(c.nbytes)
+            dev.copy_h2d(da.ptr, a)
+            dev.copy_h2d(db.ptr, b)
+            dev.gemm(desc, da.ptr, db.ptr, dc.ptr)
+            dev.copy_d2h_into(c, dc.ptr)
+            dev.stream_sync()
+            for x in (da, db, dc):
+                x.free()
+
+        t_dev = timed(device_call, 0.2)
+        t_cpu = timed(lambda: O.matmul(a, b, threads=1), 0.5)
+        rows.append({"m": m, "k": k, "n": n, "device_us": t_dev * 1e6, "cpu_us": t_cpu * 1e6,
+                     "speedup": t_cpu / t_dev})
+    cands_e = sorted({r["m"] * r["n"] for r in rows})
+    cands_w = [0] + sorted({r["m"] * r["n"] * r["k"] for r in rows})
+    rule, best = None, None
+    for e in cands_e:
+        for wk in cands_w:
+            sent = [r for r in rows if r["m"] * r["n"] >= e and r["m"] * r["n"] * r["k"] >= wk]
+            if all(r["speedup"] >= 1.0 for r in sent) and (best is None or len(sent) > best):
+                best = len(sent)
+                rule = {"element_threshold": e, "work_threshold": wk, "shapes_sent_to_device": len(sent),
+                        "shapes_faster_on_device": sum(r["speedup"] >= 1.0 for r in rows), "shapes": len(rows)}
+    emit({"metric": "host-array f32 GEMM end to end: device vs one CPU thread", "unit": "us",
+          "cpu": "oracle restatement of tensor-core gemmNT, 1 thread", "rows": rows, "rule": rule})
+
+
+def reference_line(args, w, name, threads, budget_s=150.0):
+    rates, sample, secs = [], "", []
     unit, scale = unit_of(w)
-    per = max(1.0, min(args.cpu_seconds, 150.0 / max(1, args.warmup + args.steps)))
+    per = max(1.0, min(args.cpu_seconds, budget_s / max(1, args.warmup + args.steps)))
     for i in range(args.warmup + args.steps):
-        r, sample, _ = cpu_sample_rate(w, per, threads)
+        r, sample, s = cpu_sample_rate(w, per, threads)
         if i >= args.warmup:
             rates.append(r)
+            secs.append(s)
     v = statistics.median(rates) / scale
-    line = {
+    return {
         "impl": "reference", "metric": w["metric"], "value": v, "unit": unit, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": flop_per_step(w) / (v * scale) * 1e3,
+        "ms_per_step_basis": (f"extrapolated: one step's work / the median rate of the {args.steps} timed samples "
+                              f"(each about {statistics.median(secs):.1f} s of CPU work on a part of the step)"),
         "higher_is_better": True, "scaling": "strong" if w["kind"] == "nsplit" else "weak", "vs_baseline": None,
         "dtype": "f32" if w.get("precision") == "f32" else "f64 (f32 storage)",
-        "data": "synthetic", "config": {"workload": args.workload, "description": w["desc"]},
+        "data": "synthetic", "config": {"workload": name, "description": w["desc"]},
         "cpu_baseline": {"value": v, "unit": unit, "cores": 1 if w["kind"] == "fusion" else threads, "kind": "port",
                          "sample": "per step: " + sample + ("" if w["kind"] == "fusion" else
                                    "; the oracle's restatement of tensor-core gemmNT / attention, OpenMP over "
                                    "row blocks / heads")},
         "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+
+
+def run_reference(args, w):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    threads = len(os.sched_getaffinity(0))
+    names = SECONDARY.get(args.workload, []) if not args.no_secondary and args.batch is None else []
+    budget = 150.0 / (1 + len(names))  # the whole arm stays within a few minutes
+    line = reference_line(args, w, args.workload, threads, budget)
+    if names:
+        line["secondary"] = [reference_line(args, dict(WORKLOADS[n]), n, threads, budget) for n in names]
     emit(line)
 
 
@@ -465,29 +552,37 @@ def time_region(dev, stream, fn, steps, barrier):
     return dev.elapsed_ms(e0, e1) / steps
 
 
-def run_ours(args, w):
+def pinned_copy_gbs(dev, nbytes=256 << 20, reps=5):
+    """Host<->device copy bandwidth from pinned memory (GB/s each way), CUDA events: the roofline of
+    the end-to-end leg's transfers."""
+    import numpy as np
+    h, hp = dev.pinned_array((nbytes,), np.uint8)
+    d = dev.alloc(nbytes)
+    out = {}
+    for key, fn in (("h2d_gbs", lambda: dev.copy_h2d(d.ptr, h, dev.stream)),
+                    ("d2h_gbs", lambda: dev.copy_d2h_into(h, d.ptr, dev.stream))):
+        fn()
+        e0, e1 = dev.event(), dev.event()
+        dev.record(e0, dev.stream)
+        for _ in range(reps):
+            fn()
+        dev.record(e1, dev.stream)
+        dev.stream_sync(dev.stream)
+        out[key] = nbytes * reps / (dev.elapsed_ms(e0, e1) * 1e-3) / 1e9
+    d.free()
+    dev.host_free(hp)
+    return out
+
+
+def measure_workload(args, w, name, ctx):
+    """Times one workload on this rank: device value, end to end, roofline and CPU samples.
+    Returns its JSON line's fields on rank 0, None on the other ranks."""
     import numpy as np
     import torch
 
     from tensor_cuda import _ffi as F
-    from tensor_cuda.runtime import Device
-
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    pg = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-        pg = dist
-
-    def barrier():
-        if pg:
-            pg.barrier()
-
-    dev = Device.shared(local)
-    stream = dev.stream
+    dev, stream, pg, world, rank, local, barrier, bus = (ctx[k] for k in ("dev", "stream", "pg", "world", "rank",
+                                                                         "local", "barrier", "bus"))
     g = torch.Generator(device=f"cuda:{local}")
     g.manual_seed(1234 + rank)
     extras = {}
@@ -515,12 +610,6 @@ def run_ours(args, w):
         step()
     dev.stream_sync(stream)
 
-    bus = None
-    try:
-        p = torch.cuda.get_device_properties(local)
-        bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
-    except Exception:
-        pass
     sampler = ClockSampler(bus)
     sampler.start()
     time.sleep(0.3)
@@ -653,71 +742,140 @@ def run_ours(args, w):
         if not single_out:
             outs[1].free()
         dev.destroy_stream(s_out)
+        if rank == 0:
+            # the host link's roofline: a step cannot end before its uploads have crossed (the
+            # read-back of the previous step overlaps them on the other copy engine)
+            bw = pinned_copy_gbs(dev)
+            h2d_b, d2h_b = e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"]
+            floor_ms = max(h2d_b / (bw["h2d_gbs"] * 1e9), d2h_b / (bw["d2h_gbs"] * 1e9)) * 1e3
+            e2e["host_link"] = {"h2d_gbs": bw["h2d_gbs"], "d2h_gbs": bw["d2h_gbs"],
+                                "source": "measured: 256 MiB pinned copies, CUDA events, this box",
+                                "floor_ms_per_step": floor_ms, "frac_of_floor": floor_ms / e2e["ms_per_step"]}
 
-    if rank == 0:
-        peaks = load_peaks()
-        long_region = ms_total > 2000
-        peak = peaks["bf16_tflops_sustained"] if long_region else peaks["bf16_tflops"]
-        rank_flop = flop_step / world if strong else flop_step
-        achieved = rank_flop / (ms_step * 1e-3) / scale  # one launch of the kernel per step and rank
-        if w["kind"] == "fusion":
-            roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                    "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} HBM copy",
-                    "traffic": profiled_traffic(args.workload), "algorithmic_bytes_per_launch": rank_flop,
-                    "kernel": kernel_name}
-        else:
-            roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                    "frac": achieved / peak,
-                    "peak_source": f"{peaks['source']} bf16 dense ({'sustained' if long_region else 'burst'})",
-                    "traffic": profiled_traffic(args.workload), "algorithmic_flop_per_launch": rank_flop,
-                    "kernel": kernel_name}
-        if strong and world > 1:
-            # fused GEMM + all-gather: the slower of the tensor-core time and the NVLink time of the
-            # bytes every GPU must receive ((p-1)/p of C), at the measured 770 GB/s per direction
-            c_bytes = out.nbytes
-            nv_bytes = c_bytes * (world - 1) / world
-            target_ms = max(rank_flop / (peak * 1e12), nv_bytes / 770e9) * 1e3
-            roof["nvlink"] = {"bytes_in_per_gpu": nv_bytes, "achieved_gbs": nv_bytes / (ms_step * 1e-3) / 1e9,
-                              "peak_gbs": 770.0, "peak_source": "measured peer copy per direction",
-                              "target_ms": target_ms, "frac_of_target": target_ms / ms_step}
-        if w["kind"] == "gemm" and w.get("dtype") == "f32":
-            roof["note"] = "3xTF32 issues 3 tf32 MMAs per product; tf32 dense peak is half of bf16"
-        if w["kind"] == "attention" and w["causal"]:
-            roof["note"] = "FLOP = causal half of 4*B*H*L^2*D (masked tiles are skipped)"
-        cpu = None
-        if not args.no_cpu_baseline and world == 1:
-            try:
-                threads = len(os.sched_getaffinity(0))
-                r, sample, secs = cpu_sample_rate(w, args.cpu_seconds, threads)
-                cpu = {"value": r / scale, "unit": unit, "cores": 1 if w["kind"] == "fusion" else threads,
-                       "kind": "port",
-                       "sample": sample + f" ({secs:.1f} s); the oracle's restatement of the reference's CPU path"}
-            except Exception as ex:  # reported, never required
-                cpu = {"value": None, "unit": unit, "cores": None, "kind": "port", "sample": f"failed: {ex}"}
-        par = (f"column split over {world} GPUs, all-gather fused into the GEMM epilogue (peer stores into the "
-               "shard-major view), then a local permute to row-major" if strong
-               else f"dp{world} (shards, no collective)")
-        cfg = {"workload": args.workload, "description": w["desc"], "parallelism": par}
-        if breakdown:
-            cfg["breakdown_ms_per_step"] = breakdown
-        cfg.update({k: w[k] for k in ("batch", "m", "n", "k", "heads", "seq", "head_dim", "out") if k in w})
-        if w["kind"] == "fusion":
-            cfg["expression"] = EXPRESSIONS[w.get("expression", "sigmoid_chain")][0]
-            cfg["precision"] = w.get("precision", "f64")
-        cfg["l2"] = "flushed between steps (256 MiB write)" if flush is not None else "inputs larger than L2 (126 MB)"
-        line = {
-            "metric": w["metric"], "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
-            "scaling": "strong" if strong else "weak",
-            "vs_baseline": None, "dtype": w["dtype"],
-            "data": "synthetic (seeded torch RNG on device; configuration shapes and distributions)",
-            "config": cfg, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-            "clocks": clocks,
-        }
-        emit(line)
     if extras:
         extras["fused"].destroy()
         extras["group"].destroy()
+    if rank != 0:
+        return None
+    peaks = load_peaks()
+    long_region = ms_total > 2000
+    peak = peaks["bf16_tflops_sustained"] if long_region else peaks["bf16_tflops"]
+    rank_flop = flop_step / world if strong else flop_step
+    achieved = rank_flop / (ms_step * 1e-3) / scale  # one launch of the kernel per step and rank
+    if w["kind"] == "fusion":
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} HBM copy",
+                "traffic": profiled_traffic(name), "algorithmic_bytes_per_launch": rank_flop,
+                "kernel": kernel_name}
+    else:
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "peak_source": f"{peaks['source']} bf16 dense ({'sustained' if long_region else 'burst'})",
+                "traffic": profiled_traffic(name), "algorithmic_flop_per_launch": rank_flop,
+                "kernel": kernel_name}
+    if strong and world > 1:
+        # fused GEMM + all-gather: the slower of the tensor-core time and the NVLink time of the
+        # bytes every GPU must receive ((p-1)/p of C), at the measured 770 GB/s per direction
+        c_bytes = out.nbytes
+        nv_bytes = c_bytes * (world - 1) / world
+        target_ms = max(rank_flop / (peak * 1e12), nv_bytes / 770e9) * 1e3
+        roof["nvlink"] = {"bytes_in_per_gpu": nv_bytes, "achieved_gbs": nv_bytes / (ms_step * 1e-3) / 1e9,
+                          "peak_gbs": 770.0, "peak_source": "measured peer copy per direction",
+                          "target_ms": target_ms, "frac_of_target": target_ms / ms_step}
+    if w["kind"] == "gemm" and w.get("dtype") == "f32":
+        # 3xTF32 issues three tf32 products per f32 product; tf32 runs at half the bf16 rate
+        tf32_roof = peak / 2 / 3
+        roof["note"] = "3xTF32 issues 3 tf32 MMAs per product; tf32 dense peak is half of bf16"
+        roof["tf32x3_roofline"] = {"peak": tf32_roof, "frac": achieved / tf32_roof,
+                                   "source": "the bf16 peak / 2 (tf32 rate) / 3 (tf32 products per f32 product)"}
+    if w["kind"] == "attention" and w["causal"]:
+        roof["note"] = "FLOP = causal half of 4*B*H*L^2*D (masked tiles are skipped)"
+    cpu = cpu1 = None
+    if not args.no_cpu_baseline and world == 1:
+        threads = len(os.sched_getaffinity(0))
+        for label, nthreads, secs_target in (("all host threads", threads, args.cpu_seconds),
+                                             ("restatement, 1 thread", 1, args.cpu_seconds / 2)):
+            try:
+                rt, sample, secs = cpu_sample_rate(w, secs_target, nthreads)
+                rec = {"value": rt / scale, "unit": unit, "cores": 1 if w["kind"] == "fusion" else nthreads,
+                       "kind": "port", "label": label,
+                       "sample": sample + f" ({secs:.1f} s); the oracle's restatement of the reference's CPU path"}
+            except Exception as ex:  # reported, never required
+                rec = {"value": None, "unit": unit, "cores": None, "kind": "port", "label": label,
+                       "sample": f"failed: {ex}"}
+            if nthreads == threads:
+                cpu = rec
+            else:
+                cpu1 = rec
+    par = (f"column split over {world} GPUs, all-gather fused into the GEMM epilogue (peer stores into the "
+           "shard-major view), then a local permute to row-major" if strong
+           else f"dp{world} (shards, no collective)")
+    cfg = {"workload": name, "description": w["desc"], "parallelism": par}
+    if breakdown:
+        cfg["breakdown_ms_per_step"] = breakdown
+    cfg.update({k: w[k] for k in ("batch", "m", "n", "k", "heads", "seq", "head_dim", "out") if k in w})
+    if w["kind"] == "fusion":
+        cfg["expression"] = EXPRESSIONS[w.get("expression", "sigmoid_chain")][0]
+        cfg["precision"] = w.get("precision", "f64")
+    cfg["l2"] = "flushed between steps (256 MiB write)" if flush is not None else "inputs larger than L2 (126 MB)"
+    line = {
+        "metric": w["metric"], "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong" if strong else "weak",
+        "vs_baseline": None, "dtype": w["dtype"],
+        "data": "synthetic (seeded torch RNG on device; configuration shapes and distributions)",
+        "config": cfg, "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if cpu1 is not None:
+        line["cpu_baseline_1thread"] = cpu1
+    return line
+
+
+# The default run also measures the fused-attention configuration, so the metric's second half
+# (fused-attention TFLOP/s) is in the same line.
+SECONDARY = {"batched_gemm_bf16": ["causal_attention_f16"]}
+
+
+def run_ours(args, w):
+    import torch
+
+    from tensor_cuda.runtime import Device
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+        pg = dist
+
+    def barrier():
+        if pg:
+            pg.barrier()
+
+    dev = Device.shared(local)
+    bus = None
+    try:
+        p = torch.cuda.get_device_properties(local)
+        bus = f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except Exception:
+        pass
+    ctx = {"dev": dev, "stream": dev.stream, "pg": pg, "world": world, "rank": rank, "local": local,
+           "barrier": barrier, "bus": bus}
+    line = measure_workload(args, w, args.workload, ctx)
+    extra = []
+    if not args.no_secondary and args.batch is None:
+        for sub_name in SECONDARY.get(args.workload, []):
+            sub = measure_workload(args, dict(WORKLOADS[sub_name]), sub_name, ctx)
+            if sub is not None:
+                extra.append(sub)
+    if rank == 0:
+        if extra:
+            line["secondary"] = extra
+        emit(line)
     if pg:
         pg.destroy_process_group()
 
@@ -739,6 +897,9 @@ def main():
     _RESULT = os.fdopen(os.dup(1), "w")
     os.dup2(2, 1)
     args = parse_args()
+    if args.threshold_sweep:
+        run_threshold_sweep(args)
+        return
     w = dict(WORKLOADS[args.workload])
     if args.batch is not None:
         w["batch"] = args.batch

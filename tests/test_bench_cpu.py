@@ -32,5 +32,10 @@ def test_reference_arm_line(extra):
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["config"]["workload"] == extra[1]
+    assert d["ms_per_step_basis"].startswith("extrapolated")
+    if extra[1] == "batched_gemm_bf16":  # the default workload carries the attention configuration too
+        (att,) = d["secondary"]
+        assert att["config"]["workload"] == "causal_attention_f16" and att["value"] > 0
+        assert att["impl"] == "reference" and att["unit"] == "TFLOP/s"
     if "--precision" in extra:
         assert "gelu" in d["metric"] and "f32 evaluation" in d["metric"] and d["dtype"] == "f32"
