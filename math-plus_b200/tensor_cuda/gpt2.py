@@ -105,12 +105,15 @@ class GPT2:
             self._pos[seq] = self.backend.from_host_sync(host("i32", (seq,), np.arange(seq, dtype=np.int32)))
         return self._pos[seq]
 
-    def forward(self, ids: CudaTensor) -> CudaTensor:
-        """ids i32 [B, L] -> logits bf16 [B, L, vocab]."""
+    def forward(self, ids: CudaTensor, stop_after: int | None = None) -> CudaTensor:
+        """ids i32 [B, L] -> logits bf16 [B, L, vocab]; with ``stop_after`` = n, the residual stream
+        bf16 [B, L, d_model] after the first n blocks instead (no final LayerNorm or LM head)."""
         be, cfg, w = self.backend, self.cfg, self.w
         B, L = ids.shape
         if L > cfg.n_ctx:
             raise ValueError(f"GPT2: sequence of {L} tokens is longer than the context ({cfg.n_ctx})")
+        if stop_after is not None and not 0 <= stop_after <= cfg.n_layer:
+            raise ValueError(f"GPT2: stop_after={stop_after} outside 0..{cfg.n_layer}")
         D, H, Dh = cfg.d_model, cfg.n_head, cfg.head_dim
         tok = be.embedding(w["wte"], ids)                      # [B, L, D]
         pos = be.embedding(w["wpe"], self._positions(L))      # [L, D]
@@ -118,9 +121,13 @@ class GPT2:
         x = be.reshape(s, (B * L, D))
         for t in (tok, pos, s):
             be.dispose(t)
-        for i in range(cfg.n_layer):
+        for i in range(cfg.n_layer if stop_after is None else stop_after):
             p = f"h.{i}."
             x = self._block(x, p, B, L, D, H, Dh)
+        if stop_after is not None:
+            out = be.reshape(x, (B, L, D))
+            be.dispose(x)
+            return out
         h = be.layerNorm(x, w["ln_f.weight"], w["ln_f.bias"], cfg.eps)
         be.dispose(x)
         logits = be.linear(h, w["wte"])                        # tied LM head: x . wte^T

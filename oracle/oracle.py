@@ -492,34 +492,40 @@ def round_bf16(x) -> np.ndarray:
 
 
 def gpt2_forward(w: dict, ids, n_layer: int, n_head: int, eps: float = 1e-5, store=round_bf16,
-                 threads: int = 1) -> np.ndarray:
+                 threads: int = 1, residual_in_epilogue: bool = False, stop_after: int | None = None) -> np.ndarray:
     """A GPT-2-shaped forward composed from the reference's CPU ops: token + position
     ``takeRows``, then per layer the pre-norm block of ``TransformerEncoderLayer.forward``
     (packages/tensor-autograd/src/transformer.ts:320-333, normFirst) with ``MultiheadAttention``'s
     packed in-projection and head split / merge (transformer.ts:223-241) under a causal mask,
     exact GELU, and a final LayerNorm and tied LM head (``linearNT`` with the token table).
     ``w`` holds f32 arrays under GPT-2's parameter names; ``store`` is applied to every op's
-    output (the device stores bf16). Returns logits [B, L, vocab]."""
+    output (the device stores bf16). ``residual_in_epilogue``: the two residual adds take the
+    projection's f32 result before it is stored (the device adds the residual inside the GEMM's
+    epilogue and stores once). ``stop_after``: return the residual stream [B, L, D] after that many
+    blocks instead of the logits. Returns logits [B, L, vocab]."""
     ids = np.ascontiguousarray(ids, np.int32)
     B, L = ids.shape
     D = w["wte"].shape[1]
     Dh = D // n_head
     causal = np.tril(np.ones((L, L), np.bool_)).reshape(1, 1, L, L)
+    proj_store = (lambda t: t) if residual_in_epilogue else store
     x = store(add_f32(embedding(w["wte"], ids), embedding(w["wpe"], np.arange(L, dtype=np.int32))))
     x = x.reshape(B * L, D)
-    for i in range(n_layer):
+    for i in range(n_layer if stop_after is None else stop_after):
         p = f"h.{i}."
         h = store(layer_norm(x, w[p + "ln_1.weight"], w[p + "ln_1.bias"], eps))
         qkv = store(linear(h, w[p + "attn.in_proj_weight"], w[p + "attn.in_proj_bias"], threads=threads))
         q, k, v = (np.ascontiguousarray(t) for t in np.transpose(qkv.reshape(B, L, 3, n_head, Dh), (2, 0, 3, 1, 4)))
         a = store(sdpa(q, k, v, causal, 1.0 / np.sqrt(Dh), threads=threads))
         merged = np.ascontiguousarray(np.transpose(a, (0, 2, 1, 3))).reshape(B * L, D)
-        o = store(linear(merged, w[p + "attn.out_proj.weight"], w[p + "attn.out_proj.bias"], threads=threads))
+        o = proj_store(linear(merged, w[p + "attn.out_proj.weight"], w[p + "attn.out_proj.bias"], threads=threads))
         x1 = store(add_f32(x, o))
         h2 = store(layer_norm(x1, w[p + "ln_2.weight"], w[p + "ln_2.bias"], eps))
         f = store(gelu(linear(h2, w[p + "mlp.fc.weight"], w[p + "mlp.fc.bias"], threads=threads)))
-        g = store(linear(f, w[p + "mlp.proj.weight"], w[p + "mlp.proj.bias"], threads=threads))
+        g = proj_store(linear(f, w[p + "mlp.proj.weight"], w[p + "mlp.proj.bias"], threads=threads))
         x = store(add_f32(x1, g))
+    if stop_after is not None:
+        return x.reshape(B, L, D)
     h = store(layer_norm(x, w["ln_f.weight"], w["ln_f.bias"], eps))
     return store(linear(h, w["wte"], threads=threads)).reshape(B, L, -1)
 

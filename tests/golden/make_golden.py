@@ -3,7 +3,7 @@
 
 Run here (where the math-plus checkout is mounted), never on the GPU box:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout of johnhenry/math-plus>
 
 It drives, as subprocesses and through their documented stdin/job-file interfaces:
 
@@ -347,7 +347,7 @@ def special_fixtures(ref: str) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="a checkout of the reference repository (johnhenry/math-plus)")
     ap.add_argument("--only", choices=["gemm", "attention", "differential", "special"],
                     help="regenerate one fixture file")
     args = ap.parse_args()

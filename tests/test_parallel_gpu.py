@@ -120,6 +120,58 @@ def test_one_rank_column_split_equals_the_oracle(dev, fused, layout):
         g.destroy()
 
 
+def _normal_bf16_rows(rows, cols, seed, std, block=512):
+    """[rows, cols] bf16 bits from the oracle's seeded normal generator, row blocks of `block` rows
+    seeded seed * 100003 + block index, generated on host threads (the generator releases the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+    out = np.empty((rows, cols), np.uint16)
+
+    def fill(i):
+        r0, r1 = i * block, min(rows, (i + 1) * block)
+        out[r0:r1] = O.normal_half_bits((r1 - r0) * cols, seed * 100003 + i, 0, std, True).reshape(r1 - r0, cols)
+
+    with ThreadPoolExecutor(max_workers=O.default_threads()) as ex:
+        list(ex.map(fill, range((rows + block - 1) // block)))
+    return out
+
+
+def test_column_split_at_the_large_gemm_configuration_sampled(dev):
+    """The single large GEMM configuration on one rank: A [16384, 8192] @ B [8192, 65536] bf16 -> bf16
+    through ColumnSplitGemm (fused path: peer barrier, the paired GEMM storing into the peer buffer,
+    barrier). 4096 random (i, j) entries are held to f64 dot products of the same bf16 inputs within
+    1e-2 relative / 2e-3 absolute, and to the f32-accumulation bound of the other GEMM tests; every
+    entry of C is finite."""
+    from tensor_cuda import _ffi as F
+    from tensor_cuda.parallel import ColumnSplitGemm, PeerGroup, unique_id
+    M, N, K = 16384, 65536, 8192
+    a_bits = _normal_bf16_rows(M, K, 71, 1 / np.sqrt(K))
+    b_bits = _normal_bf16_rows(K, N, 72, 1 / np.sqrt(K))
+    g = PeerGroup(dev, 0, 1, unique_id())
+    try:
+        cs = ColumnSplitGemm(g, M, N, K, "bf16", "bf16", F.B_KN, fused=True)
+        da, db = dev.upload(a_bits), dev.upload(b_bits)
+        ptr = cs(da.ptr, db.ptr)
+        dev.sync()
+        c_bits = dev.download(ptr, M * N * 2, np.uint16, (M, N))
+        cs.destroy()
+        da.free()
+        db.free()
+    finally:
+        g.destroy()
+    got_all = from_device_dtype(c_bits, "bf16")
+    assert np.isfinite(got_all).all()
+    rng = np.random.default_rng(5)
+    i = rng.integers(0, M, 4096)
+    j = rng.integers(0, N, 4096)
+    a = from_device_dtype(a_bits[i], "bf16").astype(np.float64)                            # [4096, K]
+    b = from_device_dtype(np.ascontiguousarray(b_bits[:, j].T), "bf16").astype(np.float64)  # [4096, K]
+    want = (a * b).sum(1)
+    absprod = (np.abs(a) * np.abs(b)).sum(1)
+    got = got_all[i, j].astype(np.float64)
+    assert np.all(np.abs(got - want) <= 2e-3 + 1e-2 * np.abs(want)), np.abs(got - want).max()
+    assert np.all(np.abs(got - want) <= gemm_bound(want, absprod, "bf16", "bf16"))
+
+
 def _gpu_count():
     try:
         import torch
