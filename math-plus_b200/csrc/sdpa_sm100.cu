@@ -392,12 +392,16 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
             const float2 a = fma2(v[2 * e], v[2 * e + 1], scl, scl, neg_m, neg_m);  // s*scale - m, two at once
             const __half2 x2 = __floats2half2_rn(a.x, a.y);
             const uint32_t e2 = ex2_f16x2(*reinterpret_cast<const uint32_t *>(&x2));
-            rs[e & 7] = add_f16x2_to_f32(rs[e & 7], e2);
             uint32_t packed = e2;
             if (BF) {
+              // bf16 P: the row sum adds the rounded values P.V uses, so that O / l stays a convex
+              // combination of V rows (the weights' common rounding cancels in the quotient).
               const float2 pf = __half22float2(*reinterpret_cast<const __half2 *>(&e2));
               __nv_bfloat162 v2 = __floats2bfloat162_rn(pf.x, pf.y);
               packed = *reinterpret_cast<uint32_t *>(&v2);
+              rs[e & 7] += __uint_as_float(packed << 16) + __uint_as_float(packed & 0xFFFF0000u);
+            } else {
+              rs[e & 7] = add_f16x2_to_f32(rs[e & 7], e2);
             }
             if (e < 32)
               w0[e] = packed;

@@ -60,10 +60,13 @@ gemmCapabilities = gemm_capabilities
 # sweep on other hardware before trusting these numbers.
 
 #: Output elements (m·n) below which the CPU path beat the device end to end, whatever k was.
-GEMM_ELEMENT_THRESHOLD = 64 * 64
-#: Multiply-adds (m·n·k) below which the CPU path beat the device end to end, even at
-#: m·n >= GEMM_ELEMENT_THRESHOLD.
-GEMM_WORK_THRESHOLD = 2 ** 18
+#: (Not binding on the measured shapes: the work test alone separated them.)
+GEMM_ELEMENT_THRESHOLD = 8 * 8
+#: Multiply-adds (m·n·k) below which the CPU path beat the device end to end: 96^3. The device's
+#: per-call floor from host arrays was 62-68 us (two uploads, the split prologue and GEMM, the
+#: read-back, a synchronisation); 96^3 took 76 us there against 141 us on one CPU thread, 64^3
+#: 67 against 49.
+GEMM_WORK_THRESHOLD = 96 ** 3
 
 
 def choose_gemm_backend(m: int, n: int, k: int | None = None) -> str:

@@ -1,13 +1,16 @@
 """The GPT-2-shaped forward on the B200 against the same forward composed from the oracle's
 restatements of the reference's CPU ops (linearNT, attention, layerNormRows, takeRows, geluErf),
 rounded to bf16 at every op output as the device stores it (the residual adds inside the
-projections' epilogues, as the device fuses them). Every comparison is per element:
-|got - want| <= 2e-3·rms(want) + 1e-2·|want| (the f16 / bf16 tolerance of the GEMM / attention
-path, its absolute term taken relative to the tensor's RMS since a stream's scale is not 1).
-Reduced sizes (2 layers, batch 2, 128 tokens; one full-width layer with the real 50257-token
-vocabulary), the residual stream after block 1 (layer-wise), then the full 12-layer model at 1024
-tokens against the oracle's full forward: per element, per-position checksums, and a
-bit-identical second run."""
+projections' epilogues, as the device fuses them).
+
+Every comparison is per element: |got - want| <= 8·sigma + 1e-2·|want|, where sigma is the RMS of
+what bf16 storage itself changes on these inputs (the same composition stored in bf16 against it
+stored in f32, the reference's own storage). A device that rounds one op's result the other way from
+the oracle diverges from it by about that much, and the oracle's own bf16-vs-f32 deviations reach ~5
+sigma; a wrong kernel is off by the signal's own scale (hundreds of sigma). Reduced sizes (2 layers,
+batch 2, 128 tokens; one full-width layer with the real 50257-token vocabulary), the residual stream
+after block 1 (layer-wise), then the full 12-layer model at 1024 tokens against the oracle's full
+forward: per element, per-position checksums of the logits, and a bit-identical second run."""
 import math
 
 import numpy as np
@@ -19,10 +22,20 @@ from _helpers import bf16_bits_to_f32
 pytestmark = pytest.mark.gpu
 
 
-def oracle_forward(cfg, w, ids, stop_after=None):
+def oracle_forward(cfg, w, ids, stop_after=None, f32_storage=False):
     f = {k: (bf16_bits_to_f32(v).reshape(v.shape) if v.dtype == np.uint16 else v) for k, v in w.items()}
+    kw = dict(store=lambda x: np.asarray(x, np.float32)) if f32_storage else {}
     return O.gpt2_forward(f, ids, cfg.n_layer, cfg.n_head, cfg.eps, threads=O.default_threads(),
-                          residual_in_epilogue=True, stop_after=stop_after)
+                          residual_in_epilogue=True, stop_after=stop_after, **kw)
+
+
+def storage_sigma(cfg, w, ids, want, stop_after=None):
+    """RMS of (bf16-stored composition - f32-stored composition): the rounding noise of bf16 storage."""
+    ref32 = oracle_forward(cfg, w, ids, stop_after, f32_storage=True)
+    sigma = math.sqrt(float(np.mean((want.astype(np.float64) - ref32) ** 2)))
+    rms = math.sqrt(float(np.mean(ref32.astype(np.float64) ** 2)))
+    assert sigma <= 0.02 * rms, (sigma, rms)  # the bound stays far below the signal
+    return sigma
 
 
 @pytest.fixture(scope="module")
@@ -41,11 +54,10 @@ def run_model(be, cfg, w, ids, stop_after=None):
     return bf16_bits_to_f32(out.data).reshape(out.shape)
 
 
-def within(got, want, rel=1e-2, abs_rms=2e-3):
-    """Per element: |got - want| <= abs_rms·rms(want) + rel·|want|. Returns (ok, worst ratio)."""
+def within(got, want, sigma, k=8.0, rel=1e-2):
+    """Per element: |got - want| <= k·sigma + rel·|want|. Returns (ok, worst ratio)."""
     want = want.astype(np.float64)
-    rms = math.sqrt(float(np.mean(want ** 2)))
-    ratio = np.abs(got.astype(np.float64) - want) / (abs_rms * rms + rel * np.abs(want))
+    ratio = np.abs(got.astype(np.float64) - want) / (k * sigma + rel * np.abs(want))
     return bool(np.all(ratio <= 1.0)), float(ratio.max())
 
 
@@ -64,8 +76,9 @@ def test_forward_matches_the_oracle_composition(be, dims):
     got = run_model(be, cfg, w, ids)
     want = oracle_forward(cfg, w, ids)
     assert got.shape == want.shape and np.all(np.isfinite(got))
-    ok, worst = within(got, want)
-    assert ok, worst
+    sigma = storage_sigma(cfg, w, ids, want)
+    ok, worst = within(got, want, sigma)
+    assert ok, (worst, sigma)
 
 
 @pytest.mark.parametrize("dims", [SMALL, WIDE])
@@ -81,8 +94,9 @@ def test_residual_stream_after_block_one(be, dims):
     got = run_model(be, cfg, w, ids, stop_after=1)
     want = oracle_forward(cfg, w, ids, stop_after=1)
     assert got.shape == (B, L, cfg.d_model)
-    ok, worst = within(got, want)
-    assert ok, worst
+    sigma = storage_sigma(cfg, w, ids, want, stop_after=1)
+    ok, worst = within(got, want, sigma)
+    assert ok, (worst, sigma)
 
 
 def test_full_size_forward_against_the_oracle_and_deterministic(be):
@@ -98,8 +112,9 @@ def test_full_size_forward_against_the_oracle_and_deterministic(be):
     assert a.shape == (1, 1024, cfg.vocab) and np.all(np.isfinite(a))
     assert np.array_equal(a, b)
     want = oracle_forward(cfg, w, ids)
-    ok, worst = within(a, want)
-    assert ok, worst
+    sigma = storage_sigma(cfg, w, ids, want)
+    ok, worst = within(a, want, sigma)
+    assert ok, (worst, sigma)
     cs_got, cs_want = a.astype(np.float64).sum(-1), want.astype(np.float64).sum(-1)
     cs_rms = math.sqrt(float(np.mean(cs_want ** 2)))
     assert np.abs(cs_got - cs_want).max() <= 1e-2 * cs_rms, (np.abs(cs_got - cs_want).max(), cs_rms)
