@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "gelu.cuh"
 #include "mpc_internal.h"
@@ -120,6 +121,7 @@ __device__ __forceinline__ void batch_index(const Params &p, int b, int &ia, int
 
 // alpha, +bias and GELU on one 32-column chunk of this warp's 32 rows (lane = row). The math is
 // written once; only the packing below depends on the output type.
+template <bool GELU_OK = true>
 __device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], int col0, int lane) {
   if (p.alpha != 1.0f) {
 #pragma unroll
@@ -145,9 +147,36 @@ __device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], i
       for (int j = 0; j < 32; ++j) f[j] += __shfl_sync(0xffffffffu, bl, j);
     }
   }
-  if (p.epilogue & MPC_EPI_GELU) {
+  if (GELU_OK && (p.epilogue & MPC_EPI_GELU)) {
 #pragma unroll
     for (int j = 0; j < 32; j += 2) gelu_erf_f32x2(f[j], f[j + 1]);
+  }
+}
+
+// The 16-bit residual R[b, row, col0 .. col0+31] as four 16-byte loads (rows below M, whole aligned
+// chunks; zeros otherwise).
+__device__ __forceinline__ void load_resid16(const Params &p, int b, int row, int col0, uint4 (&v)[4]) {
+  if (row < p.M && col0 + 32 <= p.N) {
+    const uint4 *r = reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(p.resid) +
+                                                     (((int64_t)b * p.M + row) * p.N + col0));
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = r[j];
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+__device__ __forceinline__ void add_resid16(float (&f)[32], const uint4 (&v)[4], bool bf) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t lo = w[e] & 0xFFFFu, hi = w[e] >> 16;
+      f[8 * j + 2 * e] += bf ? __uint_as_float(lo << 16) : __half2float(__ushort_as_half((unsigned short)lo));
+      f[8 * j + 2 * e + 1] += bf ? __uint_as_float(hi << 16) : __half2float(__ushort_as_half((unsigned short)hi));
+    }
   }
 }
 
@@ -463,94 +492,116 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + col_base;
       const int row0 = mt * C::TILE_M + static_cast<int>(rank) * C::BM + q * 32;
-      uint32_t r[32];
-      tmem_ld32(t_row, r);
+      // The chunk loop, instantiated twice: PRE prefetches a 16-bit residual one chunk ahead (for
+      // the residual epilogue without GELU, whose registers it would otherwise compete with).
+      auto chunks = [&](auto pre) {
+        constexpr bool PRE = decltype(pre)::value;
+        uint32_t r[32];
+        uint4 rv[4];
+        const int colt = nt * BN + col_base;
+        tmem_ld32(t_row, r);
+        if constexpr (PRE) load_resid16(p, b, row0 + lane, colt, rv);
 #pragma unroll 1
-      for (int c = 0; c < COLS / 32; ++c) {
-        tmem_ld_wait(r);
-        float f[32];
+        for (int c = 0; c < COLS / 32; ++c) {
+          tmem_ld_wait(r);
+          float f[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
-        if (c + 1 < COLS / 32) {
-          tmem_ld32(t_row + (c + 1) * 32, r);  // next chunk's load overlaps this chunk's math
-        } else {
-          // This warp's share of the accumulator is in registers: release it to the MMA warp.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if constexpr (PAIR)
-              mbar_arrive_cluster(acc_empty_lead + acc * 8);
-            else
-              mbar_arrive(&acc_empty[acc]);
-          }
-        }
-        const int col0 = nt * BN + col_base + c * 32;
-        epilogue_math(p, f, col0, lane);
-        if (p.epilogue & MPC_EPI_RESIDUAL) add_residual(p, f, b, row0 + lane, col0);
-        // f32: one 32 x 32 store per chunk; 16-bit: chunks pair up into one 32 x 64 store
-        const bool wide = p.out_dtype != MPC_F32;
-        const int half = wide ? (c & 1) : 0;
-        if (half == 0) {
-          if (lane == 0) tma_store_wait_read<0>();  // the previous store has finished reading the block
-          __syncwarp();
-        }
-        stage_row(buf, f, p.out_dtype, lane, half);
-        if ((!wide || half == 1) && p.c_direct) {
-          // Row by row from the staged block: the warp writes one row's 32 (f32) or 64 (16-bit)
-          // consecutive outputs per step, undoing the 128-byte swizzle.
-          __syncwarp();
-          const int cs = col0 - 32 * half;
-          // The row pointer steps by N per row and the column bounds are fixed for the block; eight
-          // rows per unrolled step (the GPT-2 LM head: 2.93 ms with four rows per step and per-row
-          // index arithmetic, 2.44 ms like this; unrolling all 32 rows gained 2% more but made the
-          // kernel spill). Half-word pairs measured faster than shifted 4-byte stores for rows
-          // starting 2 bytes past a 4-byte boundary (3.96 ms).
-          const size_t rb0 = ((size_t)b * p.M + row0) * (size_t)p.N + cs;
-          const int rows = p.M - row0 < 32 ? p.M - row0 : 32;
-          if (!wide) {
-            float *rp = static_cast<float *>(p.c_direct) + rb0;
-            const bool colok = cs + lane < p.N;
-#pragma unroll 8
-            for (int rr = 0; rr < 32; ++rr, rp += p.N) {
-              const uint32_t v = *reinterpret_cast<const uint32_t *>(buf + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4) +
-                                                                     ((lane & 3) << 2));
-              if (rr < rows && colok) rp[lane] = __uint_as_float(v);
-            }
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(r[j]);
+          if (c + 1 < COLS / 32) {
+            tmem_ld32(t_row + (c + 1) * 32, r);  // next chunk's load overlaps this chunk's math
           } else {
-            uint16_t *rp = static_cast<uint16_t *>(p.c_direct) + rb0;
-            const int c0 = cs + 2 * lane;
-            const bool ok0 = c0 < p.N, ok1 = c0 + 1 < p.N;
-#pragma unroll 8
-            for (int rr = 0; rr < 32; ++rr, rp += p.N) {
-              const uint32_t v = *reinterpret_cast<const uint32_t *>(buf + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4) +
-                                                                     ((lane & 3) << 2));
-              if (rr < rows) {
-                if (ok0) rp[2 * lane] = static_cast<uint16_t>(v & 0xffffu);
-                if (ok1) rp[2 * lane + 1] = static_cast<uint16_t>(v >> 16);
-              }
+            // This warp's share of the accumulator is in registers: release it to the MMA warp.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (PAIR)
+                mbar_arrive_cluster(acc_empty_lead + acc * 8);
+              else
+                mbar_arrive(&acc_empty[acc]);
             }
           }
-          __syncwarp();  // the block may be staged again
-        } else if (!wide || half == 1) {
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
+          const int col0 = nt * BN + col_base + c * 32;
+          if constexpr (PRE) {
+            epilogue_math<false>(p, f, col0, lane);
+            if (col0 + 32 <= p.N)
+              add_resid16(f, rv, p.out_dtype == MPC_BF16);
+            else
+              add_residual(p, f, b, row0 + lane, col0);
+            // the next chunk's residual is in flight while this chunk is staged and stored
+            if (c + 1 < COLS / 32) load_resid16(p, b, row0 + lane, colt + (c + 1) * 32, rv);
+          } else {
+            epilogue_math(p, f, col0, lane);
+            if (p.epilogue & MPC_EPI_RESIDUAL) add_residual(p, f, b, row0 + lane, col0);
+          }
+          // f32: one 32 x 32 store per chunk; 16-bit: chunks pair up into one 32 x 64 store
+          const bool wide = p.out_dtype != MPC_F32;
+          const int half = wide ? (c & 1) : 0;
+          if (half == 0) {
+            if (lane == 0) tma_store_wait_read<0>();  // the previous store has finished reading the block
+            __syncwarp();
+          }
+          stage_row(buf, f, p.out_dtype, lane, half);
+          if ((!wide || half == 1) && p.c_direct) {
+            // Row by row from the staged block: the warp writes one row's 32 (f32) or 64 (16-bit)
+            // consecutive outputs per step, undoing the 128-byte swizzle.
+            __syncwarp();
             const int cs = col0 - 32 * half;
-            if (row0 < p.M && cs < p.N) {
-              if constexpr (NDST == 1) {
-                tma_store_3d(&maps.c[0], buf, cs, row0, b);
-              } else {  // the first destination rotates with the tile and warp: spread the peers' load
-                const int first = (tile + ew) % p.ndst;
-                for (int d = 0; d < p.ndst; ++d) {
-                  const int t = first + d < p.ndst ? first + d : first + d - p.ndst;
-                  tma_store_3d(&maps.c[t], buf, cs, row0, b);
+            // The row pointer steps by N per row and the column bounds are fixed for the block; eight
+            // rows per unrolled step (the GPT-2 LM head: 2.93 ms with four rows per step and per-row
+            // index arithmetic, 2.44 ms like this; unrolling all 32 rows gained 2% more but made the
+            // kernel spill). Half-word pairs measured faster than shifted 4-byte stores for rows
+            // starting 2 bytes past a 4-byte boundary (3.96 ms).
+            const size_t rb0 = ((size_t)b * p.M + row0) * (size_t)p.N + cs;
+            const int rows = p.M - row0 < 32 ? p.M - row0 : 32;
+            if (!wide) {
+              float *rp = static_cast<float *>(p.c_direct) + rb0;
+              const bool colok = cs + lane < p.N;
+#pragma unroll 8
+              for (int rr = 0; rr < 32; ++rr, rp += p.N) {
+                const uint32_t v = *reinterpret_cast<const uint32_t *>(buf + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4) +
+                                                                       ((lane & 3) << 2));
+                if (rr < rows && colok) rp[lane] = __uint_as_float(v);
+              }
+            } else {
+              uint16_t *rp = static_cast<uint16_t *>(p.c_direct) + rb0;
+              const int c0 = cs + 2 * lane;
+              const bool ok0 = c0 < p.N, ok1 = c0 + 1 < p.N;
+#pragma unroll 8
+              for (int rr = 0; rr < 32; ++rr, rp += p.N) {
+                const uint32_t v = *reinterpret_cast<const uint32_t *>(buf + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4) +
+                                                                       ((lane & 3) << 2));
+                if (rr < rows) {
+                  if (ok0) rp[2 * lane] = static_cast<uint16_t>(v & 0xffffu);
+                  if (ok1) rp[2 * lane + 1] = static_cast<uint16_t>(v >> 16);
                 }
               }
             }
-            tma_store_commit();
+            __syncwarp();  // the block may be staged again
+          } else if (!wide || half == 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              const int cs = col0 - 32 * half;
+              if (row0 < p.M && cs < p.N) {
+                if constexpr (NDST == 1) {
+                  tma_store_3d(&maps.c[0], buf, cs, row0, b);
+                } else {  // the first destination rotates with the tile and warp: spread the peers' load
+                  const int first = (tile + ew) % p.ndst;
+                  for (int d = 0; d < p.ndst; ++d) {
+                    const int t = first + d < p.ndst ? first + d : first + d - p.ndst;
+                    tma_store_3d(&maps.c[t], buf, cs, row0, b);
+                  }
+                }
+              }
+              tma_store_commit();
+            }
           }
         }
-      }
+      };
+      if ((p.epilogue & MPC_EPI_RESIDUAL) && !(p.epilogue & MPC_EPI_GELU) && p.out_dtype != MPC_F32 && p.resid_vec)
+        chunks(std::true_type{});
+      else
+        chunks(std::false_type{});
     }
     if (lane == 0) {
       tma_store_wait_all<0>();

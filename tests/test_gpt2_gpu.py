@@ -29,9 +29,10 @@ def oracle_forward(cfg, w, ids, stop_after=None, f32_storage=False):
                           residual_in_epilogue=True, stop_after=stop_after, **kw)
 
 
-def storage_sigma(cfg, w, ids, want, stop_after=None):
+def storage_sigma(cfg, w, ids, want, stop_after=None, ref32=None):
     """RMS of (bf16-stored composition - f32-stored composition): the rounding noise of bf16 storage."""
-    ref32 = oracle_forward(cfg, w, ids, stop_after, f32_storage=True)
+    if ref32 is None:
+        ref32 = oracle_forward(cfg, w, ids, stop_after, f32_storage=True)
     sigma = math.sqrt(float(np.mean((want.astype(np.float64) - ref32) ** 2)))
     rms = math.sqrt(float(np.mean(ref32.astype(np.float64) ** 2)))
     assert sigma <= 0.02 * rms, (sigma, rms)  # the bound stays far below the signal
@@ -102,7 +103,7 @@ def test_residual_stream_after_block_one(be, dims):
 def test_full_size_forward_against_the_oracle_and_deterministic(be):
     """The full 12-layer model at 1024 tokens (one sequence) against the oracle's full forward:
     every logit within the per-element bound, the per-position checksums (sums over the
-    vocabulary) within 1e-2 of the checksums' RMS; a second run is bit-identical."""
+    vocabulary) within 8 times their own bf16 storage noise; a second run is bit-identical."""
     from tensor_cuda.gpt2 import GPT2Config, random_weights
     cfg = GPT2Config()
     w = random_weights(cfg, seed=1)
@@ -112,9 +113,13 @@ def test_full_size_forward_against_the_oracle_and_deterministic(be):
     assert a.shape == (1, 1024, cfg.vocab) and np.all(np.isfinite(a))
     assert np.array_equal(a, b)
     want = oracle_forward(cfg, w, ids)
-    sigma = storage_sigma(cfg, w, ids, want)
+    ref32 = oracle_forward(cfg, w, ids, f32_storage=True)
+    sigma = storage_sigma(cfg, w, ids, want, ref32=ref32)
     ok, worst = within(a, want, sigma)
     assert ok, (worst, sigma)
-    cs_got, cs_want = a.astype(np.float64).sum(-1), want.astype(np.float64).sum(-1)
-    cs_rms = math.sqrt(float(np.mean(cs_want ** 2)))
-    assert np.abs(cs_got - cs_want).max() <= 1e-2 * cs_rms, (np.abs(cs_got - cs_want).max(), cs_rms)
+    # per-position checksums: the same noise yardstick, taken over the checksums themselves
+    cs_got, cs_want, cs_32 = (x.astype(np.float64).sum(-1) for x in (a, want, ref32))
+    cs_sigma = math.sqrt(float(np.mean((cs_want - cs_32) ** 2)))
+    cs_rms = math.sqrt(float(np.mean(cs_32 ** 2)))
+    assert cs_sigma <= 0.1 * cs_rms, (cs_sigma, cs_rms)
+    assert np.abs(cs_got - cs_want).max() <= 8 * cs_sigma, (np.abs(cs_got - cs_want).max(), cs_sigma, cs_rms)

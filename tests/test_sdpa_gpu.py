@@ -54,6 +54,19 @@ def exact(x, dtype):
     return to_device_dtype(x, dtype)[1]
 
 
+def half_tol(q, k, v, mask, scale, want, dtype):
+    """Per-element bound for f16 / bf16 attention: 2e-3 + 1e-2·|want|, and for bf16 the effect of
+    bf16 attention weights on top: P.V multiplies probabilities rounded to 8 significant bits, which
+    moves a normalised output by at most 2 * 2^-9 times the weighted spread of the V rows it averages,
+    sqrt(E_w[v^2] - O^2) (E_w[v^2] is attention with V squared). Rows that average a few very
+    different V rows (the first rows under a causal mask) need that term; long rows barely do."""
+    tol = 2e-3 + 1e-2 * np.abs(want)
+    if dtype == "bf16":
+        ev2 = O.sdpa(q, k, (v.astype(np.float64) ** 2).astype(np.float32), mask, scale, threads=O.default_threads())
+        tol = tol + 2.0 ** -8 * np.sqrt(np.maximum(ev2.astype(np.float64) - want.astype(np.float64) ** 2, 0.0))
+    return tol
+
+
 def ref_lse(q, k, scale, causal):
     s = np.einsum("bhqd,bhkd->bhqk", q.astype(np.float64), np.repeat(k, q.shape[1] // k.shape[1], 1).astype(np.float64))
     s = s * scale
@@ -106,7 +119,7 @@ def test_differential_sdpa_cases(dev, golden_dir):
             e = [exact(x, dt) for x in ins[:3]]
             got = run_sdpa(dev, *e, dt, scale, mask=mask)
             want = O.sdpa(*e, mask, scale)
-            tol = 2e-3 + 1e-2 * np.abs(want)
+            tol = half_tol(*e, mask, scale, want, dt)
             assert np.all(np.abs(got - want) <= tol), (name, dt, np.abs(got - want).max())
 
 
@@ -127,8 +140,8 @@ def test_tensor_core_path_shapes(dev, dtype, B, H, Hk, Lq, Lk, D, causal):
     got, lse = run_sdpa(dev, q, k, v, dtype, scale, causal=causal, want_lse=True)
     mask = np.tril(np.ones((Lq, Lk), np.bool_)).reshape(1, 1, Lq, Lk) if causal else None
     want = O.sdpa(q, k, v, mask, scale, threads=O.default_threads())
-    tol = 2e-3 + 1e-2 * np.abs(want)
-    assert np.all(np.abs(got - want) <= tol), np.abs(got - want).max()
+    tol = half_tol(q, k, v, mask, scale, want, dtype)
+    assert np.all(np.abs(got - want) <= tol), float((np.abs(got - want) / tol).max())
     assert np.abs(lse - ref_lse(q, k, scale, causal)).max() <= 2e-3
 
 
@@ -210,6 +223,5 @@ def test_packed_qkv_layout_matches_the_contiguous_oracle(dev, dtype, D, causal):
     q, k, v = (np.ascontiguousarray(np.transpose(x[:, :, i].astype(np.float32), (0, 2, 1, 3))) for i in range(3))
     mask = np.tril(np.ones((L, L), np.bool_)).reshape(1, 1, L, L) if causal else None
     want = np.transpose(O.sdpa(q, k, v, mask, 1 / np.sqrt(D), threads=O.default_threads()), (0, 2, 1, 3))
-    tol = {"f32": 1e-5 + 1e-5 * np.abs(want), "f16": 2e-3 + 1e-2 * np.abs(want),
-           "bf16": 2e-3 + 1e-2 * np.abs(want)}[dtype]
+    tol = 1e-5 + 1e-5 * np.abs(want) if dtype == "f32" else half_tol(q, k, v, mask, 1 / np.sqrt(D), want, dtype)
     assert np.all(np.abs(got - want) <= tol), np.abs(got - want).max()
