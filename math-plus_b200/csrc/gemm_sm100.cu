@@ -262,7 +262,9 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], in
 // bytes on the even CTA's `full` barrier), holds its 128 rows of the accumulator in its own tensor
 // memory and runs its own epilogue; the even CTA's MMA commits release both CTAs' slots and
 // accumulators, and both CTAs' epilogue warps release the accumulator on the even CTA.
-template <int KIND, bool B_MN, int BN, int STAGES, int NDST, bool PAIR>
+// RES16: the epilogue adds a 16-bit residual (no GELU), loading each chunk's residual while the chunk
+// before it is stored; a separate instantiation so that the other epilogues keep their registers.
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST, bool PAIR, bool RES16 = false>
 __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ MapsT<NDST> maps, const Params p) {
   using C = Cfg<KIND, B_MN, BN, STAGES, PAIR>;
   extern __shared__ uint8_t smem_raw[];
@@ -492,8 +494,8 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN + col_base;
       const int row0 = mt * C::TILE_M + static_cast<int>(rank) * C::BM + q * 32;
-      // The chunk loop, instantiated twice: PRE prefetches a 16-bit residual one chunk ahead (for
-      // the residual epilogue without GELU, whose registers it would otherwise compete with).
+      // The chunk loop; PRE (the RES16 kernel) has each chunk's 16-bit residual loaded while the chunk
+      // before it is staged and stored.
       auto chunks = [&](auto pre) {
         constexpr bool PRE = decltype(pre)::value;
         uint32_t r[32];
@@ -598,7 +600,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
           }
         }
       };
-      if ((p.epilogue & MPC_EPI_RESIDUAL) && !(p.epilogue & MPC_EPI_GELU) && p.out_dtype != MPC_F32 && p.resid_vec)
+      if constexpr (RES16)
         chunks(std::true_type{});
       else
         chunks(std::false_type{});
@@ -689,10 +691,10 @@ __global__ void fill_epilogue_kernel(void *C, int out_dtype, int64_t rows, int64
   }
 }
 
-template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1, bool PAIR = false>
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1, bool PAIR = false, bool RES16 = false>
 int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream_t st) {
   using C = Cfg<KIND, B_MN, BN, STAGES, PAIR>;
-  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST, PAIR>;
+  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST, PAIR, RES16>;
   static bool configured[64] = {};
   static int pairs_resident[64] = {};
   const int ord = dev->ordinal & 63;
@@ -936,10 +938,19 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
                         128 / (uint32_t)eo, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st))) return rc;
+  const bool res16 = (p.epilogue & MPC_EPI_RESIDUAL) && !(p.epilogue & MPC_EPI_GELU) && eo == 2 && p.resid_vec;
   if (pr.tf32 && pr.BN == 64)
     rc = launch<kTF32x3, false, 64, 4>(dev, maps, p, st);
   else if (pr.tf32)
     rc = launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
+  else if (res16 && pr.pair && pr.b_mn)
+    rc = launch<kHalf, true, 256, 6, 1, true, true>(dev, maps, p, st);
+  else if (res16 && pr.pair)
+    rc = launch<kHalf, false, 256, 6, 1, true, true>(dev, maps, p, st);
+  else if (res16 && pr.b_mn)
+    rc = launch<kHalf, true, 256, 4, 1, false, true>(dev, maps, p, st);
+  else if (res16)
+    rc = launch<kHalf, false, 256, 4, 1, false, true>(dev, maps, p, st);
   else if (pr.pair && pr.b_mn)
     rc = launch<kHalf, true, 256, 6, 1, true>(dev, maps, p, st);
   else if (pr.pair)

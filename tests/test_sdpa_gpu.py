@@ -222,6 +222,8 @@ def test_packed_qkv_layout_matches_the_contiguous_oracle(dev, dtype, D, causal):
     got = np.asarray(got, np.float32).reshape(B, L, H, D)
     q, k, v = (np.ascontiguousarray(np.transpose(x[:, :, i].astype(np.float32), (0, 2, 1, 3))) for i in range(3))
     mask = np.tril(np.ones((L, L), np.bool_)).reshape(1, 1, L, L) if causal else None
-    want = np.transpose(O.sdpa(q, k, v, mask, 1 / np.sqrt(D), threads=O.default_threads()), (0, 2, 1, 3))
-    tol = 1e-5 + 1e-5 * np.abs(want) if dtype == "f32" else half_tol(q, k, v, mask, 1 / np.sqrt(D), want, dtype)
+    want_h = O.sdpa(q, k, v, mask, 1 / np.sqrt(D), threads=O.default_threads())  # [B, H, L, D]
+    want = np.transpose(want_h, (0, 2, 1, 3))
+    tol = (1e-5 + 1e-5 * np.abs(want) if dtype == "f32"
+           else np.transpose(half_tol(q, k, v, mask, 1 / np.sqrt(D), want_h, dtype), (0, 2, 1, 3)))
     assert np.all(np.abs(got - want) <= tol), np.abs(got - want).max()
