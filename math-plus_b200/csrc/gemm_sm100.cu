@@ -56,7 +56,27 @@ struct Params {
   int resid_vec;       // resid rows start 16-byte aligned (vector loads)
   void *c_direct;      // non-null: C [batch, M, N] whose rows are not 16-byte aligned, written with
                        // plain stores from the staged block instead of TMA
+  int splits;          // 3xTF32: K halves per output tile (1 or 2); with 2 the halves add into a zeroed C
+  int kb_split;        // K blocks per half
 };
+
+// Work unit u of the persistent loop: its output tile and K-block range. Only the 3xTF32 kernel splits
+// K (two halves of one tile on different SMs, reduce-added into C); everything else has one unit per tile.
+template <int KIND>
+__device__ __forceinline__ void unit_range(const Params &p, int u, int &tile, int &kb0, int &kb1, bool &first) {
+  if constexpr (KIND == kTF32x3) {
+    const int sp = u % p.splits;
+    tile = u / p.splits;
+    kb0 = sp * p.kb_split;
+    kb1 = min(kb0 + p.kb_split, p.k_blocks);
+    first = sp == 0;
+  } else {
+    tile = u;
+    kb0 = 0;
+    kb1 = p.k_blocks;
+    first = true;
+  }
+}
 
 // The operand maps and NDST output maps; each 32 x 32 output block is stored through c[0..ndst).
 template <int NDST>
@@ -122,12 +142,13 @@ __device__ __forceinline__ void batch_index(const Params &p, int b, int &ia, int
 // alpha, +bias and GELU on one 32-column chunk of this warp's 32 rows (lane = row). The math is
 // written once; only the packing below depends on the output type.
 template <bool GELU_OK = true>
-__device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], int col0, int lane) {
+__device__ __forceinline__ void epilogue_math(const Params &p, float (&f)[32], int col0, int lane,
+                                              bool add_bias = true) {
   if (p.alpha != 1.0f) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) f[j] *= p.alpha;
   }
-  if (p.epilogue & MPC_EPI_BIAS) {
+  if ((p.epilogue & MPC_EPI_BIAS) && add_bias) {
     // Every lane adds the same 32 bias values: uniform 16-byte loads (one broadcast each) when the
     // chunk is whole and aligned, else one load per lane and shuffles.
     if (col0 + 32 <= p.N && !(reinterpret_cast<uintptr_t>(p.bias + col0) & 15)) {
@@ -336,12 +357,14 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int tile = first_tile; ok && tile < p.tiles_total; tile += tile_step) {
-        int b, mt, nt, ia, ib;
+      for (int u = first_tile; ok && u < p.tiles_total; u += tile_step) {
+        int tile, kb0, kb1, b, mt, nt, ia, ib;
+        bool first;
+        unit_range<KIND>(p, u, tile, kb0, kb1, first);
         tile_coords(p, tile, b, mt, nt);
         batch_index(p, b, ia, ib);
         const int m_base = mt * C::TILE_M + static_cast<int>(rank) * C::BM;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitProducer, p.timeout_ns)) {
             ok = false;
             break;
@@ -416,13 +439,16 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = first_tile; ok && tile < p.tiles_total; tile += tile_step, ++local) {
+      for (int u = first_tile; ok && u < p.tiles_total; u += tile_step, ++local) {
+        int tile, kb0, kb1;
+        bool first;
+        unit_range<KIND>(p, u, tile, kb0, kb1, first);
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, abort_flag, p.err, kErrWaitAccEmpty, p.timeout_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns)) {
             ok = false;
             break;
@@ -435,7 +461,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
             const uint64_t ad = make_sdesc(a_addr + ks * (C::UK * C::ES), 16, 1024);
             const uint64_t bd = B_MN ? make_sdesc(b_addr + ks * (C::UK * 128), C::BK * 128, 1024)
                                      : make_sdesc(b_addr + ks * (C::UK * C::ES), 16, 1024);
-            const uint32_t accum = (kb | ks) ? 1u : 0u;
+            const uint32_t accum = (kb != kb0 || ks) ? 1u : 0u;
             if constexpr (PAIR) {
               mma_f16_ss_pair(d_tmem, ad, bd, idesc_rt, accum);
             } else if constexpr (KIND == kHalf) {
@@ -485,8 +511,10 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
     const int col_base = (ew >> 2) * COLS;
     uint8_t *buf = epi + ew * 4096;
     int local = 0;
-    for (int tile = first_tile; tile < p.tiles_total; tile += tile_step, ++local) {
-      int b, mt, nt;
+    for (int u = first_tile; u < p.tiles_total; u += tile_step, ++local) {
+      int tile, kb0, kb1, b, mt, nt;
+      bool first;
+      unit_range<KIND>(p, u, tile, kb0, kb1, first);
       tile_coords(p, tile, b, mt, nt);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
@@ -532,7 +560,7 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
             // the next chunk's residual is in flight while this chunk is staged and stored
             if (c + 1 < COLS / 32) load_resid16(p, b, row0 + lane, colt + (c + 1) * 32, rv);
           } else {
-            epilogue_math(p, f, col0, lane);
+            epilogue_math(p, f, col0, lane, first);  // a second K half adds no bias
             if (p.epilogue & MPC_EPI_RESIDUAL) add_residual(p, f, b, row0 + lane, col0);
           }
           // f32: one 32 x 32 store per chunk; 16-bit: chunks pair up into one 32 x 64 store
@@ -585,7 +613,12 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
             if (lane == 0) {
               const int cs = col0 - 32 * half;
               if (row0 < p.M && cs < p.N) {
-                if constexpr (NDST == 1) {
+                if constexpr (KIND == kTF32x3) {
+                  if (p.splits > 1)  // the two K halves add into C (zeroed before the launch)
+                    tma_reduce_add_3d(&maps.c[0], buf, cs, row0, b);
+                  else
+                    tma_store_3d(&maps.c[0], buf, cs, row0, b);
+                } else if constexpr (NDST == 1) {
                   tma_store_3d(&maps.c[0], buf, cs, row0, b);
                 } else {  // the first destination rotates with the tile and warp: spread the peers' load
                   const int first = (tile + ew) % p.ndst;
@@ -758,12 +791,13 @@ struct Prep {
   bool tf32 = false, b_mn = false;
   bool pair = false;  // CTA pairs: 256 x 256 tiles, two SMs per tile
   int BN = 256;
+  int splits = 1;     // 3xTF32: 2 = each 128 x 128 tile's K in two halves, reduce-added into a zeroed C
 };
 
 // Validates `d` and fills every kernel parameter that does not depend on the output.
 // Returns MPC_OK with prep.batch == 0 (or M / N == 0) when there is nothing to compute.
 static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, const char *who, Params &p, Prep &pr,
-                   bool allow_pair = false) {
+                   bool allow_pair = false, bool c_tma = false) {
   const int64_t M = d->m, N = d->n, K = d->k;
   if (M < 0 || N < 0 || K < 0)
     return fail(MPC_ERR_INVALID, "%s: negative dimension m=%lld n=%lld k=%lld", who, (long long)M, (long long)N,
@@ -798,8 +832,17 @@ static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, c
   pr.tf32 = d->dtype_in == MPC_F32;
   pr.b_mn = !pr.tf32 && d->b_layout == MPC_B_KN;
   pr.BN = pr.tf32 ? 128 : 256;
-  // 3xTF32 on a problem with fewer 128 x 128 tiles than SMs: 128 x 64 tiles keep more SMs busy.
-  if (pr.tf32 && pr.batch * ((M + 127) / 128) * ((N + 127) / 128) < dev->prop.multiProcessorCount) pr.BN = 64;
+  // 3xTF32 on a problem with fewer 128 x 128 tiles than SMs: the two K halves of each tile on two SMs
+  // (f32 C written through TMA, no GELU / residual, at least 8 K blocks per tile: the halves add into
+  // a zeroed C, and with two addends the sum is the same whichever lands first), else 128 x 64 tiles.
+  const int64_t tiles128 = pr.batch * ((M + 127) / 128) * ((N + 127) / 128);
+  if (pr.tf32 && tiles128 < dev->prop.multiProcessorCount) {
+    if (c_tma && d->dtype_out == MPC_F32 && !(d->epilogue & (MPC_EPI_GELU | MPC_EPI_RESIDUAL)) && (K + 31) / 32 >= 8 &&
+        2 * tiles128 <= dev->prop.multiProcessorCount)
+      pr.splits = 2;
+    else
+      pr.BN = 64;
+  }
   // f16 / bf16 with at least one 256 x 256 tile per resident pair: CTA pairs (half the B bytes
   // per SM, a third less operand traffic per product than 128 x 256 tiles on one SM).
   pr.pair = allow_pair && !pr.tf32 &&
@@ -809,10 +852,12 @@ static int prepare(mpc_device *dev, const mpc_gemm_desc *d, const float *bias, c
   p.K = (int)K;
   p.tiles_m = (int)((M + (pr.pair ? 255 : 127)) / (pr.pair ? 256 : 128));
   p.tiles_n = (int)((N + pr.BN - 1) / pr.BN);
-  const int64_t tiles = pr.batch * p.tiles_m * p.tiles_n;
+  const int64_t tiles = pr.batch * p.tiles_m * p.tiles_n * pr.splits;
   if (tiles > INT32_MAX) return fail(MPC_ERR_UNSUPPORTED, "%s: %lld tiles", who, (long long)tiles);
-  p.tiles_total = (int)tiles;
+  p.tiles_total = (int)tiles;  // work units: tiles x K splits
   p.k_blocks = (int)((K + (pr.tf32 ? 31 : 63)) / (pr.tf32 ? 32 : 64));
+  p.splits = pr.splits;
+  p.kb_split = (p.k_blocks + pr.splits - 1) / pr.splits;
   p.group_m = 16;
   p.alpha = d->alpha;
   p.bias = bias;
@@ -904,7 +949,8 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
   using namespace gemm;
   Params p;
   Prep pr;
-  int rc = prepare(dev, d, bias, "mpc_gemm", p, pr, true);
+  const bool c_tma = !((uintptr_t)Cout & 15) && (d->n * (int64_t)dtype_size(d->dtype_out)) % 16 == 0;
+  int rc = prepare(dev, d, bias, "mpc_gemm", p, pr, true, c_tma);
   if (rc) return rc;
   const int64_t M = d->m, N = d->n, K = d->k, batch = pr.batch;
   if ((d->epilogue & MPC_EPI_RESIDUAL) && !resid)
@@ -938,6 +984,7 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
                         128 / (uint32_t)eo, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
   if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st))) return rc;
+  if (pr.splits > 1) MPC_CUDA(dev, cudaMemsetAsync(Cout, 0, (size_t)(batch * M * N) * 4, st));  // K halves add into it
   const bool res16 = (p.epilogue & MPC_EPI_RESIDUAL) && !(p.epilogue & MPC_EPI_GELU) && eo == 2 && p.resid_vec;
   if (pr.tf32 && pr.BN == 64)
     rc = launch<kTF32x3, false, 64, 4>(dev, maps, p, st);
@@ -1100,7 +1147,7 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
   Prep pr;
   // The same validation and kernel choice as mpc_gemm's f32 path (tile limits, the 128 x 64 tiles
   // for problems with fewer 128 x 128 tiles than SMs).
-  if ((rc = prepare(dev, d, bias, who, p, pr))) return rc;
+  if ((rc = prepare(dev, d, bias, who, p, pr, false, true))) return rc;  // C goes out through TMA (staged if need be)
   const int64_t M = d->m, N = d->n, K = d->k, batch = pr.batch;
   if (batch == 0 || M == 0 || N == 0) return MPC_OK;
   if (!A || !B || !Cout) return fail(MPC_ERR_INVALID, "%s: null operand pointer", who);
@@ -1142,6 +1189,8 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
       (rc = make_map_3d(&maps.b_lo, f32, b_lo, K, N, pr.nB, ldk * 4, N * ldk * 4, 32, pr.BN, SW)) ||
       (rc = make_map_3d(&maps.c[0], f32, cdst, N, M, batch, ldc * 4, M * ldc * 4, 32, 32, SW)))
     return rc;
+  if (pr.splits > 1)  // the two K halves of each tile add into it
+    MPC_CUDA(dev, cudaMemsetAsync(cdst, 0, (size_t)(batch * M * ldc) * 4, st));
   rc = pr.BN == 64 ? launch<kTF32x3, false, 64, 4>(dev, maps, p, st) : launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
   if (rc) return rc;
   if (stage_c)
