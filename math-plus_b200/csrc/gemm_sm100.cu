@@ -670,17 +670,37 @@ __device__ __forceinline__ float to_tf32(float x) {
   return __uint_as_float(r);
 }
 
-// Row-major [rows, cols] -> [rows, ld] hi / lo (columns cols..ld-1 zero).
+// Row-major [rows, cols] -> [rows, ld] hi / lo (columns cols..ld-1 zero). Rows walk blockIdx.y and
+// columns blockIdx.x / threadIdx.x, so no element index is divided; when the rows need no padding
+// (ld == cols) and the source is 16-byte aligned, whole float4s move instead.
 __global__ void split_rows_kernel(const float *__restrict__ src, float *__restrict__ hi, float *__restrict__ lo,
                                   int64_t rows, int64_t cols, int64_t ld) {
-  const int64_t total = rows * ld;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / ld, c = i - r * ld;
-    const float x = c < cols ? src[r * cols + c] : 0.0f;
-    const float h = to_tf32(x);
-    hi[i] = h;
-    lo[i] = to_tf32(x - h);
+  if (ld == cols && !(reinterpret_cast<uintptr_t>(src) & 15) && (cols & 3) == 0) {
+    const int64_t n4 = rows * cols / 4;
+    const int64_t stride = (int64_t)gridDim.x * gridDim.y * blockDim.x;
+    for (int64_t i = ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+      const float4 x = reinterpret_cast<const float4 *>(src)[i];
+      const float4 h = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
+      reinterpret_cast<float4 *>(hi)[i] = h;
+      reinterpret_cast<float4 *>(lo)[i] =
+          make_float4(to_tf32(x.x - h.x), to_tf32(x.y - h.y), to_tf32(x.z - h.z), to_tf32(x.w - h.w));
+    }
+    return;
   }
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < ld; c += (int64_t)gridDim.x * blockDim.x) {
+      const float x = c < cols ? src[r * cols + c] : 0.0f;
+      const float h = to_tf32(x);
+      hi[r * ld + c] = h;
+      lo[r * ld + c] = to_tf32(x - h);
+    }
+}
+
+// The launch shape of split_rows_kernel: about 8 blocks of 256 threads per SM.
+static inline dim3 split_rows_grid(int64_t rows, int64_t ld) {
+  const int64_t gx = (ld + 255) / 256 < 8 ? (ld + 255) / 256 : 8;
+  const int64_t gy = rows < 148 * 8 / gx ? rows : 148 * 8 / gx;
+  return dim3((unsigned)(gx > 0 ? gx : 1), (unsigned)(gy > 0 ? gy : 1));
 }
 
 // [nb][K][N] -> [nb][N][ld] hi / lo, transposing through a 32x33 shared tile.
@@ -888,11 +908,11 @@ static int operand_maps(mpc_device *dev, const mpc_gemm_desc *d, const Prep &pr,
     if ((rc = s.a.get(dev, st, (size_t)(nA * M * ldk) * 4)) || (rc = s.a2.get(dev, st, (size_t)(nA * M * ldk) * 4)) ||
         (rc = s.b.get(dev, st, (size_t)(nB * N * ldk) * 4)) || (rc = s.b2.get(dev, st, (size_t)(nB * N * ldk) * 4)))
       return rc;
-    split_rows_kernel<<<1184, 256, 0, st>>>(static_cast<const float *>(A), (float *)s.a.ptr, (float *)s.a2.ptr,
+    split_rows_kernel<<<split_rows_grid(nA * M, ldk), 256, 0, st>>>(static_cast<const float *>(A), (float *)s.a.ptr, (float *)s.a2.ptr,
                                             nA * M, K, ldk);
     dev->launches++;
     if (d->b_layout == MPC_B_NK) {
-      split_rows_kernel<<<1184, 256, 0, st>>>(static_cast<const float *>(B), (float *)s.b.ptr, (float *)s.b2.ptr,
+      split_rows_kernel<<<split_rows_grid(nB * N, ldk), 256, 0, st>>>(static_cast<const float *>(B), (float *)s.b.ptr, (float *)s.b2.ptr,
                                               nB * N, K, ldk);
     } else {
       dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)nB);
@@ -1171,9 +1191,9 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
   float *b_hi = reinterpret_cast<float *>(scratch + 2 * a_plane);
   float *b_lo = reinterpret_cast<float *>(scratch + 2 * a_plane + b_plane);
   float *cdst = stage_c ? reinterpret_cast<float *>(scratch + 2 * a_plane + 2 * b_plane) : Cout;
-  split_rows_kernel<<<1184, 256, 0, st>>>(A, a_hi, a_lo, pr.nA * M, K, ldk);
+  split_rows_kernel<<<split_rows_grid(pr.nA * M, ldk), 256, 0, st>>>(A, a_hi, a_lo, pr.nA * M, K, ldk);
   if (d->b_layout == MPC_B_NK) {
-    split_rows_kernel<<<1184, 256, 0, st>>>(B, b_hi, b_lo, pr.nB * N, K, ldk);
+    split_rows_kernel<<<split_rows_grid(pr.nB * N, ldk), 256, 0, st>>>(B, b_hi, b_lo, pr.nB * N, K, ldk);
   } else {
     dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)pr.nB);
     split_transpose_kernel<<<g, dim3(32, 8), 0, st>>>(B, b_hi, b_lo, (int)K, (int)N, (int)ldk);
