@@ -86,7 +86,7 @@ struct MapsT {
 using Maps = MapsT<1>;
 constexpr int kMaxDst = 8;
 
-template <int KIND, bool B_MN, int BN, int STAGES, bool PAIR = false, bool SHARE = false>
+template <int KIND, bool B_MN, int BN, int STAGES, bool PAIR = false>
 struct Cfg {
   static constexpr int BM = 128;                   // rows of A / C per CTA
   static constexpr int TILE_M = PAIR ? 256 : 128;  // rows of one output tile (a CTA pair shares one)
@@ -100,7 +100,7 @@ struct Cfg {
   static constexpr int NOPS = KIND == kHalf ? 1 : 2;
   static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
   static constexpr int EPI_WARPS = 8;
-  static constexpr int THREADS = 32 * (2 + EPI_WARPS + (SHARE ? 1 : 0));  // SHARE: + the A-copy warp
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS);
   static constexpr int EPI_BYTES = EPI_WARPS * 4096;  // one 32-row x 128-byte staging block per warp
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
@@ -122,21 +122,6 @@ __device__ __forceinline__ void tile_coords(const Params &p, int tile, int &b, i
   const int rg = r - g * group;
   mt = first_m + rg % gm;
   nt = rg / gm;
-}
-
-// SHARE: unit `tile` is a pair of adjacent column tiles (the same rows of A); `half` picks one.
-__device__ __forceinline__ void tile_coords_cols2(const Params &p, int tile, int half, int &b, int &mt, int &nt) {
-  const int tn2 = p.tiles_n >> 1;
-  const int per_batch = p.tiles_m * tn2;
-  b = tile / per_batch;
-  const int r = tile - b * per_batch;
-  const int group = p.group_m * tn2;
-  const int g = r / group;
-  const int first_m = g * p.group_m;
-  const int gm = min(p.tiles_m - first_m, p.group_m);
-  const int rg = r - g * group;
-  mt = first_m + rg % gm;
-  nt = 2 * (rg / gm) + half;
 }
 
 __device__ __forceinline__ void batch_index(const Params &p, int b, int &ia, int &ib) {
@@ -300,17 +285,9 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], in
 // accumulators, and both CTAs' epilogue warps release the accumulator on the even CTA.
 // RES16: the epilogue adds a 16-bit residual (no GELU), loading each chunk's residual while the chunk
 // before it is stored; a separate instantiation so that the other epilogues keep their registers.
-// SHARE (with PAIR): clusters of four CTAs, two pairs computing two adjacent column tiles of the same
-// rows. Each row half of A crosses from L2 once per cluster instead of once per pair: CTA 0 loads the
-// upper 128 rows and copies them into CTA 2's shared memory, CTA 3 loads the lower 128 rows and
-// copies them into CTA 1's (shared-memory bulk copies within the cluster), so the cluster reads 3/4
-// of the operand bytes a pair-per-tile grid reads. A slot is free for reuse once both pairs' MMAs
-// have read it.
-template <int KIND, bool B_MN, int BN, int STAGES, int NDST, bool PAIR, bool RES16 = false, bool SHARE = false>
-// (384 for SHARE's 11 warps keeps the register cap at 168, what three warps of one SM sub-partition allow)
-__global__ void __launch_bounds__(SHARE ? 384 : 320, 1)
-    gemm_kernel(const __grid_constant__ MapsT<NDST> maps, const Params p) {
-  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR, SHARE>;
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST, bool PAIR, bool RES16 = false>
+__global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ MapsT<NDST> maps, const Params p) {
+  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *stages = smem;
@@ -320,36 +297,18 @@ __global__ void __launch_bounds__(SHARE ? 384 : 320, 1)
   uint64_t *acc_full = empty + STAGES;
   uint64_t *acc_empty = acc_full + 2;
   uint64_t *drain = acc_empty + 2;
-  uint64_t *a_local = drain + 1;       // SHARE: this CTA's own A load of a slot landed
-  uint64_t *fwd_full = a_local + STAGES;  // SHARE: the A rows copied in from the other pair landed
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(SHARE ? fwd_full + STAGES : drain + 1);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int CLUSTER = SHARE ? 4 : (PAIR ? 2 : 1);
-  const uint32_t crank = PAIR ? cluster_ctarank() : 0;  // rank in the cluster
-  const uint32_t rank = crank & 1;                      // 0: the CTA of its pair that issues the MMAs
-  const uint32_t lead = crank & ~1u;                    // cluster rank of this pair's MMA-issuing CTA
-  const int pair_id = SHARE ? static_cast<int>(crank >> 1) : 0;
-  const int first_tile = static_cast<int>(blockIdx.x) / CLUSTER;
-  const int tile_step = static_cast<int>(gridDim.x) / CLUSTER;
-  auto coords = [&](int tile, int &b, int &mt, int &nt) {
-    if constexpr (SHARE)
-      tile_coords_cols2(p, tile, pair_id, b, mt, nt);
-    else
-      tile_coords(p, tile, b, mt, nt);
-  };
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0;  // 0: the CTA that issues the MMAs
+  const int first_tile = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int tile_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      // SHARE: `full` also takes one arrival for each of the pair's two A halves (loaded here or copied
-      // in), and `empty` one commit from each pair's MMAs.
-      mbar_init(&full[s], SHARE ? 3 : 1);
-      mbar_init(&empty[s], SHARE ? 2 : 1);
-      if constexpr (SHARE) {
-        mbar_init(&a_local[s], 1);
-        mbar_init(&fwd_full[s], 1);
-      }
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
@@ -386,15 +345,10 @@ __global__ void __launch_bounds__(SHARE ? 384 : 320, 1)
   const uint32_t tmem_base = *tmem_slot;
   // Cluster addresses: the even CTA's `full` and `acc_empty` barriers (where both CTAs count),
   // and the odd CTA's `empty` and `acc_full` barriers (which the even CTA's commits release).
-  const uint32_t full_lead = PAIR ? cluster_addr(full, lead) : 0;
-  const uint32_t acc_empty_lead = PAIR ? cluster_addr(acc_empty, lead) : 0;
-  const uint32_t empty_odd = PAIR ? cluster_addr(empty, lead | 1) : 0;
-  const uint32_t acc_full_odd = PAIR ? cluster_addr(acc_full, lead | 1) : 0;
-  // SHARE: the other pair's two CTAs (whose slots this pair's MMAs also release), and whether this
-  // CTA loads its A rows (ranks 0 and 3, copying them to rank ^ 2) or receives them (ranks 1 and 2).
-  const uint32_t empty_other0 = SHARE ? cluster_addr(empty, lead ^ 2) : 0;
-  const uint32_t empty_other1 = SHARE ? cluster_addr(empty, (lead ^ 2) | 1) : 0;
-  const bool a_loader = SHARE && (crank == 0 || crank == 3);
+  const uint32_t full_lead = PAIR ? cluster_addr(full, 0) : 0;
+  const uint32_t acc_empty_lead = PAIR ? cluster_addr(acc_empty, 0) : 0;
+  const uint32_t empty_odd = PAIR ? cluster_addr(empty, 1) : 0;
+  const uint32_t acc_full_odd = PAIR ? cluster_addr(acc_full, 1) : 0;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -407,7 +361,7 @@ __global__ void __launch_bounds__(SHARE ? 384 : 320, 1)
         int tile, kb0, kb1, b, mt, nt, ia, ib;
         bool first;
         unit_range<KIND>(p, u, tile, kb0, kb1, first);
-        coords(tile, b, mt, nt);
+        tile_coords(p, tile, b, mt, nt);
         batch_index(p, b, ia, ib);
         const int m_base = mt * C::TILE_M + static_cast<int>(rank) * C::BM;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -418,19 +372,11 @@ __global__ void __launch_bounds__(SHARE ? 384 : 320, 1)
           uint8_t *sa = stages + stage * C::STAGE_BYTES;
           uint8_t *sb = sa + C::A_BYTES;
           if constexpr (PAIR) {
-            // Both CTAs' bytes complete the even CTA's barrier, which the even CTA arms. SHARE: only
-            // B's bytes; A goes to this CTA's own barrier (a_local) when it loads A at all.
-            if (rank == 0) mbar_expect_tx(&full[stage], SHARE ? 2 * C::B_BYTES : 2 * C::STAGE_BYTES);
+            // Both CTAs' bytes complete the even CTA's barrier, which the even CTA arms.
+            if (rank == 0) mbar_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
             const uint32_t bar = full_lead + stage * 8;
             const int n_base = nt * BN + static_cast<int>(rank) * C::BNL;
-            if constexpr (SHARE) {
-              if (a_loader) {
-                mbar_expect_tx(&a_local[stage], C::A_BYTES);
-                tma_load_3d(&maps.a, &a_local[stage], sa, kb * C::BK, m_base, ia);
-              }
-            } else {
-              tma_load_3d_pair(&maps.a, bar, sa, kb * C::BK, m_base, ia);
-            }
+            tma_load_3d_pair(&maps.a, bar, sa, kb * C::BK, m_base, ia);
             if constexpr (B_MN) {
 #pragma unroll
               for (int j = 0; j < C::BNL / 64; ++j)
@@ -485,44 +431,6 @@ __global__ void __launch_bounds__(SHARE ? 384 : 320, 1)
         }
       }
     }
-  } else if (SHARE && warp == C::THREADS / 32 - 1) {
-    if (lane == 0) {
-      // ---------------- SHARE: A rows across the two pairs ----------------
-      // A loader: once its A load of a slot has landed, copy it into the same slot of rank ^ 2 and
-      // tell this pair's MMA-issuing CTA. A receiver: arm its copy-in barrier, wait for the copy,
-      // and tell this pair's MMA-issuing CTA.
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      const uint32_t peer = crank ^ 2;
-      bool armed = false;  // a receiver's copy-in barrier is armed for the current phase
-      for (int u = first_tile; ok && u < p.tiles_total; u += tile_step) {
-        int tile, kb0, kb1;
-        bool first;
-        unit_range<KIND>(p, u, tile, kb0, kb1, first);
-        for (int kb = kb0; kb < kb1; ++kb) {
-          uint8_t *sa = stages + stage * C::STAGE_BYTES;
-          if (a_loader) {
-            if (!(ok = mbar_wait(&a_local[stage], phase, abort_flag, p.err, kErrWaitProducer, p.timeout_ns))) break;
-            bulk_copy_to_cluster(cluster_addr(sa, peer), sa, C::A_BYTES, cluster_addr(&fwd_full[stage], peer));
-          } else {
-            mbar_expect_tx(&fwd_full[stage], C::A_BYTES);
-            armed = true;
-            if (!(ok = mbar_wait(&fwd_full[stage], phase, abort_flag, p.err, kErrWaitProducer, p.timeout_ns))) break;
-            armed = false;
-          }
-          mbar_arrive_cluster(full_lead + stage * 8);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
-          }
-        }
-      }
-      if (!ok && armed) {  // an armed copy-in may still be on its way: let it land first
-        volatile int never = 0;
-        mbar_wait(&fwd_full[stage], phase, &never, p.err, kErrWaitProducer, p.timeout_ns);
-      }
-    }
   } else if (warp == 1) {
     // ---------------- MMA issuer (one thread; the even CTA's for a pair) ----------------
     if (lane == 0 && rank == 0) {
@@ -571,10 +479,6 @@ __global__ void __launch_bounds__(SHARE ? 384 : 320, 1)
           if constexpr (PAIR) {  // the slot is free in both CTAs once these MMAs have read it
             tc_commit_pair(smem_u32(&empty[stage]));
             tc_commit_pair(empty_odd + stage * 8);
-            if constexpr (SHARE) {  // ... and, for the A rows it shares, in the other pair's CTAs
-              tc_commit_pair(empty_other0 + stage * 8);
-              tc_commit_pair(empty_other1 + stage * 8);
-            }
           } else {
             tc_commit(&empty[stage]);  // the slot is free once these MMAs have read it
           }
@@ -611,7 +515,7 @@ __global__ void __launch_bounds__(SHARE ? 384 : 320, 1)
       int tile, kb0, kb1, b, mt, nt;
       bool first;
       unit_range<KIND>(p, u, tile, kb0, kb1, first);
-      coords(tile, b, mt, nt);
+      tile_coords(p, tile, b, mt, nt);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait_warp(&acc_full[acc], acc_phase, abort_flag, p.err, kErrWaitAccFull, p.timeout_ns)) break;
@@ -840,12 +744,10 @@ __global__ void fill_epilogue_kernel(void *C, int out_dtype, int64_t rows, int64
   }
 }
 
-template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1, bool PAIR = false, bool RES16 = false,
-          bool SHARE = false>
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1, bool PAIR = false, bool RES16 = false>
 int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream_t st) {
-  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR, SHARE>;
-  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST, PAIR, RES16, SHARE>;
-  constexpr int CLUSTER = SHARE ? 4 : 2;
+  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR>;
+  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST, PAIR, RES16>;
   static bool configured[64] = {};
   static int pairs_resident[64] = {};
   const int ord = dev->ordinal & 63;
@@ -854,12 +756,11 @@ int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream
     configured[ord] = true;
   }
   if constexpr (PAIR) {
-    // One persistent pair per TPC that can hold one (SHARE: one cluster of two pairs per two TPCs):
-    // as many clusters as fit at once.
+    // One persistent pair per TPC that can hold one: as many clusters of two as fit at once.
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CLUSTER;
+    attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.blockDim = dim3(C::THREADS);
@@ -868,14 +769,14 @@ int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     if (!pairs_resident[ord]) {
-      cfg.gridDim = dim3(CLUSTER * (dev->prop.multiProcessorCount / CLUSTER));
+      cfg.gridDim = dim3(2 * (dev->prop.multiProcessorCount / 2));
       int n = 0;
       MPC_CUDA(dev, cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
-      if (n < 1) return fail(MPC_ERR_UNSUPPORTED, "gemm_kernel: no cluster of %d CTAs fits on this device", CLUSTER);
+      if (n < 1) return fail(MPC_ERR_UNSUPPORTED, "gemm_kernel: no CTA pair fits on this device");
       pairs_resident[ord] = n;
     }
-    const int clusters = p.tiles_total < pairs_resident[ord] ? p.tiles_total : pairs_resident[ord];
-    cfg.gridDim = dim3(CLUSTER * clusters);
+    const int pairs = p.tiles_total < pairs_resident[ord] ? p.tiles_total : pairs_resident[ord];
+    cfg.gridDim = dim3(2 * pairs);
     MPC_CUDA(dev, cudaLaunchKernelEx(&cfg, kern, maps, p));
   } else {
     const int grid = p.tiles_total < dev->prop.multiProcessorCount ? p.tiles_total : dev->prop.multiProcessorCount;
@@ -888,9 +789,6 @@ int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream
 }  // namespace gemm
 
 // ---- host entry -----------------------------------------------------------------------------
-// Whether eligible f16 / bf16 problems run two CTA pairs per cluster sharing A's rows (SHARE).
-constexpr bool kShareA = false;
-
 static CUtensorMapDataType tmap_dtype(int dt) {
   switch (dt) {
     case MPC_F32:
@@ -1108,11 +1006,6 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
   if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st))) return rc;
   if (pr.splits > 1) MPC_CUDA(dev, cudaMemsetAsync(Cout, 0, (size_t)(batch * M * N) * 4, st));  // K halves add into it
   const bool res16 = (p.epilogue & MPC_EPI_RESIDUAL) && !(p.epilogue & MPC_EPI_GELU) && eo == 2 && p.resid_vec;
-  // Two pairs per cluster sharing A's rows: an even number of column tiles, and at least one pair of
-  // tiles for every cluster of four the GPU holds at once.
-  const bool share = kShareA && pr.pair && !res16 && p.tiles_n % 2 == 0 &&
-                     p.tiles_total / 2 >= dev->prop.multiProcessorCount / 4;
-  if (share) p.tiles_total /= 2;  // units are pairs of column tiles
   if (pr.tf32 && pr.BN == 64)
     rc = launch<kTF32x3, false, 64, 4>(dev, maps, p, st);
   else if (pr.tf32)
@@ -1125,10 +1018,6 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
     rc = launch<kHalf, true, 256, 4, 1, false, true>(dev, maps, p, st);
   else if (res16)
     rc = launch<kHalf, false, 256, 4, 1, false, true>(dev, maps, p, st);
-  else if (share && pr.b_mn)
-    rc = launch<kHalf, true, 256, 6, 1, true, false, true>(dev, maps, p, st);
-  else if (share)
-    rc = launch<kHalf, false, 256, 6, 1, true, false, true>(dev, maps, p, st);
   else if (pr.pair && pr.b_mn)
     rc = launch<kHalf, true, 256, 6, 1, true>(dev, maps, p, st);
   else if (pr.pair)

@@ -178,14 +178,6 @@ __device__ __forceinline__ void tma_load_3d_pair(const CUtensorMap *map, uint32_
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
-// A bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory into another CTA of the
-// cluster (dst: cluster address), completing on an mbarrier of that CTA (cluster address). Not a load
-// from global memory: the source is this CTA's own shared memory.
-__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "r"(smem_u32(src)), "r"(bytes), "r"(bar)
-               : "memory");
-}
 // Tensor memory of a pair: executed by one warp (the same warp index) in each CTA; the same
 // columns are allocated in both CTAs and the base address is written to both CTAs' *dst_smem.
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {

@@ -260,45 +260,3 @@ def test_gemm_cta_pair_tiles(dev, b_layout, dtype_in, dtype_out, epi, n, m, b_sh
         bound = gemm_bound(want, absprod, dtype_in, dtype_out) + (1e-5 * (1 + np.abs(want)) if "gelu" in epi else 0)
         assert np.all(np.abs(got[i] - want) <= bound), i
 
-
-@pytest.mark.parametrize("b_layout,dtype_in,dtype_out,epi,n,m,b_shared", [
-    ("kn", "bf16", "f32", "bias+gelu", 1900, 1000, False),  # column and row tails
-    ("nk", "f16", "bf16", "", 2048, 1030, True),            # one B for every batch entry
-    ("kn", "bf16", "bf16", "bias", 1930, 1000, False),      # rows not 16-byte aligned: plain stores
-])
-def test_gemm_pairs_sharing_a(dev, b_layout, dtype_in, dtype_out, epi, n, m, b_shared):
-    """Problems with an even number of 256-column tiles and at least one pair of tiles per cluster
-    of four CTAs run two CTA pairs per cluster on adjacent column tiles, the A rows loaded once per
-    cluster and copied between the pairs' shared memories: batched (6 entries), with row, column
-    and K tails, both B layouts, against the oracle."""
-    from tensor_cuda import _ffi as F
-    from tensor_cuda.runtime import gemm_desc
-    bsz, k = 6, 200
-    lay = F.B_NK if b_layout == "nk" else F.B_KN
-    a_up, a_ex = to_device_dtype(O.lcg_gemm(bsz * m * k, 61).reshape(bsz, m, k), dtype_in)
-    b_shape = (n, k) if b_layout == "nk" else (k, n)
-    nb = 1 if b_shared else bsz
-    b_up, b_ex = to_device_dtype(O.lcg_gemm(nb * n * k, 62).reshape((nb,) + b_shape), dtype_in)
-    bias = O.normal_f32(n, 63, 0, 0.5)
-    flags = (F.EPI_BIAS if "bias" in epi else 0) | (F.EPI_GELU if "gelu" in epi else 0)
-    eo = F.DTYPE_BYTES[F.DTYPE_CODES[dtype_out]]
-    desc = gemm_desc(m, n, k, F.DTYPE_CODES[dtype_in], F.DTYPE_CODES[dtype_out], lay, flags, 1.0, (bsz,), (m * k,),
-                     (0 if b_shared else n * k,))
-    da, db, dbias = dev.upload(a_up), dev.upload(b_up), dev.upload(bias)
-    dc = dev.alloc(bsz * m * n * eo)
-    dev.gemm(desc, da.ptr, db.ptr, dc.ptr, dbias.ptr if flags else None)
-    dev.sync()
-    got = from_device_dtype(dev.download(dc.ptr, bsz * m * n * eo, NP_STORAGE[dtype_out], (bsz * m * n,)),
-                            dtype_out).reshape(bsz, m, n).astype(np.float64)
-    for i in range(bsz):
-        bi = b_ex[0 if b_shared else i]
-        bt = bi.T if b_layout == "nk" else bi
-        want = a_ex[i].astype(np.float64) @ bt.astype(np.float64)
-        absprod = np.abs(a_ex[i]).astype(np.float64) @ np.abs(bt).astype(np.float64)
-        if "bias" in epi:
-            want = want + bias
-            absprod = absprod + np.abs(bias)
-        if "gelu" in epi:
-            want = O.gelu(want.astype(np.float32)).astype(np.float64)
-        bound = gemm_bound(want, absprod, dtype_in, dtype_out) + (1e-5 * (1 + np.abs(want)) if "gelu" in epi else 0)
-        assert np.all(np.abs(got[i] - want) <= bound), (i, float(np.abs(got[i] - want).max()))
