@@ -12,7 +12,12 @@
 //               warps per lane quadrant split the columns), apply alpha / +bias / exact-erf GELU,
 //               convert, stage 32-row x 128-byte swizzled blocks in shared memory and TMA-store
 //               them (bounds clipped by the tensor map)
-// Two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1.
+// Two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1. The linear
+// (B K-major) kernel on CTA pairs gives each epilogue warp two staging blocks (5 stages instead of 6
+// to make room), so a block is staged while the store of the one before it still reads: with
+// K = 768 (GPT-2's projections) the epilogue is no longer hidden, and out-proj + residual took
+// 58.5 us against 64.1, fc + GELU 176.5 against 180.6 (the matmul kernel of the batched
+// configuration keeps 6 stages and one block: it measured slower the other way).
 //
 // Operand layouts, all with the 128-byte swizzle:
 //   A        K-major (row-major [M,K]); box {BK, 128}
@@ -86,7 +91,7 @@ struct MapsT {
 using Maps = MapsT<1>;
 constexpr int kMaxDst = 8;
 
-template <int KIND, bool B_MN, int BN, int STAGES, bool PAIR = false>
+template <int KIND, bool B_MN, int BN, int STAGES, bool PAIR = false, int EPI_BUFS = 1>
 struct Cfg {
   static constexpr int BM = 128;                   // rows of A / C per CTA
   static constexpr int TILE_M = PAIR ? 256 : 128;  // rows of one output tile (a CTA pair shares one)
@@ -101,7 +106,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = NOPS * (A_BYTES + B_BYTES);
   static constexpr int EPI_WARPS = 8;
   static constexpr int THREADS = 32 * (2 + EPI_WARPS);
-  static constexpr int EPI_BYTES = EPI_WARPS * 4096;  // one 32-row x 128-byte staging block per warp
+  static constexpr int EPI_BYTES = EPI_WARPS * 4096 * EPI_BUFS;  // EPI_BUFS 32-row x 128-byte staging blocks per warp
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
@@ -285,9 +290,9 @@ __device__ __forceinline__ void stage_row(uint8_t *buf, const float (&f)[32], in
 // accumulators, and both CTAs' epilogue warps release the accumulator on the even CTA.
 // RES16: the epilogue adds a 16-bit residual (no GELU), loading each chunk's residual while the chunk
 // before it is stored; a separate instantiation so that the other epilogues keep their registers.
-template <int KIND, bool B_MN, int BN, int STAGES, int NDST, bool PAIR, bool RES16 = false>
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST, bool PAIR, bool RES16 = false, int EPI_BUFS = 1>
 __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ MapsT<NDST> maps, const Params p) {
-  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR>;
+  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR, EPI_BUFS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *stages = smem;
@@ -509,7 +514,9 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
     const int q = warp & 3;  // TMEM lane quadrant this warp may access (hardware rule: warp % 4)
     constexpr int COLS = BN / 2;  // each of the two warps of a quadrant takes half the columns
     const int col_base = (ew >> 2) * COLS;
-    uint8_t *buf = epi + ew * 4096;
+    uint8_t *const buf0 = epi + ew * 4096 * EPI_BUFS;
+    uint8_t *buf = buf0;
+    int nblk = 0;  // staging blocks this warp has filled (the next one is nblk % EPI_BUFS)
     int local = 0;
     for (int u = first_tile; u < p.tiles_total; u += tile_step, ++local) {
       int tile, kb0, kb1, b, mt, nt;
@@ -567,7 +574,9 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
           const bool wide = p.out_dtype != MPC_F32;
           const int half = wide ? (c & 1) : 0;
           if (half == 0) {
-            if (lane == 0) tma_store_wait_read<0>();  // the previous store has finished reading the block
+            buf = buf0 + (nblk % EPI_BUFS) * 4096;
+            ++nblk;
+            if (lane == 0) tma_store_wait_read<EPI_BUFS - 1>();  // the store that last read this block is done
             __syncwarp();
           }
           stage_row(buf, f, p.out_dtype, lane, half);
@@ -744,10 +753,10 @@ __global__ void fill_epilogue_kernel(void *C, int out_dtype, int64_t rows, int64
   }
 }
 
-template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1, bool PAIR = false, bool RES16 = false>
+template <int KIND, bool B_MN, int BN, int STAGES, int NDST = 1, bool PAIR = false, bool RES16 = false, int EPI_BUFS = 1>
 int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream_t st) {
-  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR>;
-  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST, PAIR, RES16>;
+  using C = Cfg<KIND, B_MN, BN, STAGES, PAIR, EPI_BUFS>;
+  auto kern = gemm_kernel<KIND, B_MN, BN, STAGES, NDST, PAIR, RES16, EPI_BUFS>;
   static bool configured[64] = {};
   static int pairs_resident[64] = {};
   const int ord = dev->ordinal & 63;
@@ -1012,8 +1021,8 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
     rc = launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
   else if (res16 && pr.pair && pr.b_mn)
     rc = launch<kHalf, true, 256, 6, 1, true, true>(dev, maps, p, st);
-  else if (res16 && pr.pair)
-    rc = launch<kHalf, false, 256, 6, 1, true, true>(dev, maps, p, st);
+  else if (res16 && pr.pair)  // linear on pairs: two staging blocks per epilogue warp
+    rc = launch<kHalf, false, 256, 5, 1, true, true, 2>(dev, maps, p, st);
   else if (res16 && pr.b_mn)
     rc = launch<kHalf, true, 256, 4, 1, false, true>(dev, maps, p, st);
   else if (res16)
@@ -1021,7 +1030,7 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
   else if (pr.pair && pr.b_mn)
     rc = launch<kHalf, true, 256, 6, 1, true>(dev, maps, p, st);
   else if (pr.pair)
-    rc = launch<kHalf, false, 256, 6, 1, true>(dev, maps, p, st);
+    rc = launch<kHalf, false, 256, 5, 1, true, false, 2>(dev, maps, p, st);
   else if (pr.b_mn)
     rc = launch<kHalf, true, 256, 4>(dev, maps, p, st);
   else

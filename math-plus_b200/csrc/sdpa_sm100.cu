@@ -23,6 +23,7 @@
 // CUDA cores, online softmax in f32 — the role of backend-webgpu's generic sdpa kernel.
 #include <algorithm>
 #include <cfloat>
+#include <vector>
 
 #include "mpc_internal.h"
 #include "sm100.cuh"
@@ -65,7 +66,7 @@ struct Cfg {
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-__device__ __forceinline__ int last_kv(const Params &p, int q0t) {
+__host__ __device__ __forceinline__ int last_kv(const Params &p, int q0t) {
   // Last KV tile any row of the Q tile starting at q0t may see.
   int last_key = p.Lk - 1;
   if (p.causal) last_key = min(last_key, min(q0t + 127, p.Lq - 1));
@@ -85,17 +86,32 @@ struct Unit {
   int last0, last1, n_kv;
 };
 
-// Units are numbered head-major; within a head the q-blocks alternate heavy and light
-// (QB-1, 0, QB-2, 1, ...), and each CTA takes units in pairs (2i, 2i+1), so under a causal mask
-// every pair carries the same work. Returns false past the last unit.
+// The k-th unit of this CTA. Pairs (SNAKE false): units are numbered head-major; within a head the
+// q-blocks alternate heavy and light (QB-1, 0, QB-2, 1, ...), and each CTA takes units in pairs
+// (2i, 2i+1), so under a causal mask every pair carries the same work (head-major order keeps a
+// head's K / V in L2). Snake (SNAKE true, chosen by the host under a causal mask when the pairs do
+// not divide evenly over the CTAs): units sorted by work, heaviest first (the last q-blocks of
+// every head, then the ones before), dealt to the CTAs in rounds that alternate direction, so the
+// CTAs' sums stay within about one unit of each other. Returns false past the last unit.
+template <bool SNAKE>
 __device__ __forceinline__ bool unit_of(const Params &p, int k, Unit &w) {
   // 32-bit arithmetic: the host keeps 2 * n_units + 2 * gridDim.x below 2^31.
-  const unsigned u = 2u * (blockIdx.x + (unsigned)(k >> 1) * gridDim.x) + (unsigned)(k & 1);
-  if (u >= (unsigned)p.n_units) return false;
   const unsigned qbn = (unsigned)p.q_blocks;
-  w.bh = (int)(u / qbn);
-  const int r = (int)(u - (unsigned)w.bh * qbn);
-  const int qb = (r & 1) ? (r >> 1) : qbn - 1 - (r >> 1);
+  int qb;
+  if constexpr (SNAKE) {
+    const unsigned n = (unsigned)k * gridDim.x + ((k & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
+    if (n >= (unsigned)p.n_units) return false;
+    const unsigned bhn = (unsigned)p.n_units / qbn;
+    const unsigned cls = n / bhn;
+    w.bh = (int)(n - cls * bhn);
+    qb = (int)(qbn - 1 - cls);
+  } else {
+    const unsigned u = 2u * (blockIdx.x + (unsigned)(k >> 1) * gridDim.x) + (unsigned)(k & 1);
+    if (u >= (unsigned)p.n_units) return false;
+    w.bh = (int)(u / qbn);
+    const int r = (int)(u - (unsigned)w.bh * qbn);
+    qb = (r & 1) ? (r >> 1) : (int)qbn - 1 - (r >> 1);
+  }
   w.b = w.bh / p.H;
   w.h = w.bh - w.b * p.H;
   w.kvh = w.h / p.rep;
@@ -120,7 +136,7 @@ __device__ __forceinline__ void load_rows(const CUtensorMap *map, uint64_t *bar,
 
 // BF: bf16 operands (P is packed as bf16), else f16. A template parameter, not a run-time flag, so
 // that the softmax's inner loops carry no per-element branch on the type.
-template <int D, bool BF>
+template <int D, bool BF, bool SNAKE>
 __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Maps maps, const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -184,7 +200,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
       int ring = 0, q_loads = 0;
       bool ok = true;
       Unit w;
-      for (int k = 0; ok && unit_of(p, k, w); ++k) {
+      for (int k = 0; ok && unit_of<SNAKE>(p, k, w); ++k) {
         // Q of the previous unit is free once its last QK products have run.
         if (k > 0 && !(ok = mbar_wait(q_empty, (k - 1) & 1, abort_flag, p.err, kErrWaitProducer, p.timeout_ns)))
           break;
@@ -242,7 +258,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
                          p.timeout_ns);
       };
       Unit w;
-      for (int k = 0; ok && unit_of(p, k, w); ++k) {
+      for (int k = 0; ok && unit_of<SNAKE>(p, k, w); ++k) {
         auto need = [&](int t, int j) { return j <= (t ? w.last1 : w.last0); };
         const int base = ring;  // K_j is ring item base + 2j, V_j item base + 2j + 1
         auto do_pv = [&](int t, int j, int sv, int &cnt) -> bool {
@@ -305,7 +321,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
     int pv_cnt = 0;  // PV products of this Q tile completed before the current unit (o_ready phases)
     bool ok = true;
     Unit w;
-    for (int k = 0; ok && unit_of(p, k, w); ++k) {
+    for (int k = 0; ok && unit_of<SNAKE>(p, k, w); ++k) {
       const int q = w.q0 + 128 * t + row;
       const int last = t ? w.last1 : w.last0;
       const bool tile_valid = t == 0 || w.valid1;
@@ -568,27 +584,61 @@ __global__ void attn_generic_kernel(const GenericParams p) {
   if (p.lse && lane == 0) p.lse[row_id] = l > 0.0f ? m + logf(l) : -INFINITY;
 }
 
-template <int D, bool BF>
-int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
+// Whether the snake order (unit_of<true>) spreads a causal launch's work more evenly than the pairs: the
+// largest per-CTA sum of unit costs (KV tiles of both Q tiles, plus one for the unit's output) under
+// each order, the snake kept when it is at least 3% lower. Beyond 2^16 units the pairs' rounding
+// loss is below half a percent and the pairs stay.
+static bool prefer_snake(const Params &p, long long grid_pairs, long long grid_snake) {
+  if (p.n_units > (1 << 16) || grid_pairs <= 0 || grid_snake <= 0) return false;
+  const int qbn = p.q_blocks;
+  const long long bhn = p.n_units / qbn;
+  std::vector<long long> cost(qbn);
+  for (int qb = 0; qb < qbn; ++qb) {
+    const int q0 = qb * 256;
+    const bool valid1 = q0 + 128 < p.Lq;
+    cost[qb] = (last_kv(p, q0) + 1) + (valid1 ? last_kv(p, q0 + 128) + 1 : 0) + 1;
+  }
+  std::vector<long long> a(grid_pairs, 0), b(grid_snake, 0);
+  for (long long u = 0; u < p.n_units; ++u) {
+    const int r = (int)(u % qbn);
+    a[(u / 2) % grid_pairs] += cost[(r & 1) ? (r >> 1) : qbn - 1 - (r >> 1)];
+    const long long k = u / grid_snake, i = u % grid_snake;
+    b[(k & 1) ? grid_snake - 1 - i : i] += cost[qbn - 1 - (int)(u / bhn)];
+  }
+  const long long ma = *std::max_element(a.begin(), a.end()), mb = *std::max_element(b.begin(), b.end());
+  return mb * 100 < ma * 97;
+}
+
+template <int D, bool BF, bool SNAKE>
+int launch_order(mpc_device *dev, const Maps &maps, const Params &p, long long grid, cudaStream_t st) {
   using C = Cfg<D>;
   static bool configured[64] = {};
   const int ord = dev->ordinal & 63;
   if (!configured[ord]) {
-    MPC_CUDA(dev, cudaFuncSetAttribute(attn_kernel<D, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    MPC_CUDA(dev, cudaFuncSetAttribute(attn_kernel<D, BF, SNAKE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaFuncAttributes fa;
-    MPC_CUDA(dev, cudaFuncGetAttributes(&fa, attn_kernel<D, BF>));
+    MPC_CUDA(dev, cudaFuncGetAttributes(&fa, attn_kernel<D, BF, SNAKE>));
     // The register split inside the kernel is sized for a 168-register launch; refuse anything else
     // rather than launch a split whose increase could never be granted.
     if (fa.numRegs != 168)
       return fail(MPC_ERR_UNSUPPORTED, "attn_kernel built with %d registers per thread (expected 168)", fa.numRegs);
     configured[ord] = true;
   }
-  // Persistent: one CTA per SM (at most), each taking pairs of units until none is left.
-  const long long pairs = ((long long)p.n_units + 1) / 2;
-  const long long grid = pairs < dev->prop.multiProcessorCount ? pairs : dev->prop.multiProcessorCount;
-  attn_kernel<D, BF><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(maps, p);
+  attn_kernel<D, BF, SNAKE><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(maps, p);
   dev->launches++;
   return check_launch(dev, "attn_kernel");
+}
+
+// Persistent: one CTA per SM (at most), each taking units until none is left; the unit order is a
+// separate instantiation so that the pairs' kernel carries no branch for the other order.
+template <int D, bool BF>
+int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
+  const long long sms = dev->prop.multiProcessorCount;
+  const long long pairs = ((long long)p.n_units + 1) / 2;
+  const long long grid = pairs < sms ? pairs : sms;
+  const long long grid_snake = p.n_units < sms ? p.n_units : sms;
+  if (p.causal && prefer_snake(p, grid, grid_snake)) return launch_order<D, BF, true>(dev, maps, p, grid_snake, st);
+  return launch_order<D, BF, false>(dev, maps, p, grid, st);
 }
 
 }  // namespace attn
