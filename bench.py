@@ -86,7 +86,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="batched_gemm_bf16", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=20,
+                    help="streamed end-to-end steps (the pipeline fills and drains once per region)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="time only --workload (the default run also times the causal attention configuration)")
@@ -693,10 +694,10 @@ def measure_workload(args, w, name, ctx):
 
     # ---- e2e: through the C ABI from pinned host buffers, copies inside the timed region ----
     # Every step copies its inputs host -> device, runs the same step and copies its result device ->
-    # host. Streaming order: inputs and the step on the device's stream, the read-back on a second
-    # stream, device buffers double-buffered, so the read-back of step i overlaps the uploads of step
-    # i + 1 (the two copy directions run on separate copy engines). The region ends when the last
-    # read-back has landed in host memory.
+    # host. Streaming order: uploads on one stream, the step on the device's stream, the read-back on
+    # a third, device buffers double-buffered, so the uploads of step i + 1 and the read-back of step i
+    # run at once on the two copy engines while step i + 1 waits only for its own uploads. The region
+    # starts before the first upload and ends when the last read-back has landed in host memory.
     e2e = None
     if args.e2e_steps > 0:
         hins = []
@@ -708,17 +709,22 @@ def measure_workload(args, w, name, ctx):
         hout, hop = dev.pinned_array((out.nbytes,), np.uint8)
         single_out = w["kind"] in ("nsplit", "gpt2")  # their output buffer is owned by the step itself
         outs = [out, out] if single_out else [out, dev.alloc(out.nbytes)]
-        s_out = dev.new_stream()
+        s_in, s_out = dev.new_stream(), dev.new_stream()
+        done_up = [dev.event(), dev.event()]
         done_step = [dev.event(), dev.event()]
         done_read = [dev.event(), dev.event()]
         step_no = [0]
 
         def e2e_step():
             k = step_no[0] & 1
+            # the uploads overwrite input buffers that the step two back read (an event never
+            # recorded counts as complete)
+            dev.wait_event(s_in, done_step[k])
             for h, _, dbuf in hins:
-                dev.copy_h2d(dbuf[k].ptr, h, stream)
+                dev.copy_h2d(dbuf[k].ptr, h, s_in)
+            dev.record(done_up[k], s_in)
+            dev.wait_event(stream, done_up[k])
             # the step overwrites an output buffer whose earlier read-back must have finished
-            # (an event never recorded counts as complete)
             dev.wait_event(stream, done_read[k ^ 1] if single_out else done_read[k])
             launch([dbuf[k].ptr for _, _, dbuf in hins], outs[k].ptr, stream)
             dev.record(done_step[k], stream)
@@ -729,25 +735,25 @@ def measure_workload(args, w, name, ctx):
 
         for _ in range(2):
             e2e_step()
-        dev.stream_sync(s_out)
-        dev.stream_sync(stream)
+        for s_ in (s_in, stream, s_out):
+            dev.stream_sync(s_)
         barrier()
         x0, x1 = dev.event(), dev.event()
-        dev.record(x0, stream)
+        dev.record(x0, s_in)
         for _ in range(args.e2e_steps):
             e2e_step()
         dev.wait_event(s_out, done_step[(step_no[0] - 1) & 1])
         dev.record(x1, s_out)
-        dev.stream_sync(s_out)
-        dev.stream_sync(stream)
+        for s_ in (s_in, stream, s_out):
+            dev.stream_sync(s_)
         barrier()
         ms_e2e = max_over_ranks(dev.elapsed_ms(x0, x1))
         e2e = {"value": job_flop / (ms_e2e / args.e2e_steps * 1e-3) / scale, "unit": unit,
                "h2d_bytes_per_step": int(sum(h.nbytes for h, _, _ in hins)), "d2h_bytes_per_step": int(hout.nbytes),
                "ms_per_step": ms_e2e / args.e2e_steps,
                "path": "per step: mpc_memcpy_h2d_async of every input -> the step -> mpc_memcpy_d2h_async of the "
-                       "result into pinned host memory; read-back on a second stream overlapping the next step's "
-                       "uploads (double-buffered device buffers)"}
+                       "result into pinned host memory; uploads, steps and read-backs on three streams, so the "
+                       "uploads of step i + 1 overlap the read-back of step i (double-buffered device buffers)"}
         for _, hp, dbuf in hins:
             dev.host_free(hp)
             for d in dbuf:
@@ -756,6 +762,7 @@ def measure_workload(args, w, name, ctx):
         if not single_out:
             outs[1].free()
         dev.destroy_stream(s_out)
+        dev.destroy_stream(s_in)
         if rank == 0:
             # the host link's roofline: a step cannot end before its uploads have crossed (the
             # read-back of the previous step overlaps them on the other copy engine)

@@ -348,6 +348,9 @@ __global__ void __launch_bounds__(320, 1) gemm_kernel(const __grid_constant__ Ma
     __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // 3xTF32 launches overlap their set-up with the split prologue (programmatic dependent launch):
+  // the hi / lo planes and C's zeros are read only after the prologue has completed.
+  if constexpr (KIND == kTF32x3) grid_dependency_wait();
   // Cluster addresses: the even CTA's `full` and `acc_empty` barriers (where both CTAs count),
   // and the odd CTA's `empty` and `acc_full` barriers (which the even CTA's commits release).
   const uint32_t full_lead = PAIR ? cluster_addr(full, 0) : 0;
@@ -679,15 +682,36 @@ __device__ __forceinline__ float to_tf32(float x) {
   return __uint_as_float(r);
 }
 
-// Row-major [rows, cols] -> [rows, ld] hi / lo (columns cols..ld-1 zero). Rows walk blockIdx.y and
-// columns blockIdx.x / threadIdx.x, so no element index is divided; when the rows need no padding
-// (ld == cols) and the source is 16-byte aligned, whole float4s move instead.
-__global__ void split_rows_kernel(const float *__restrict__ src, float *__restrict__ hi, float *__restrict__ lo,
-                                  int64_t rows, int64_t cols, int64_t ld) {
+// The 3xTF32 prologue, one launch: A's rows split into hi / lo planes, B's rows split (B [N,K]) or
+// B [K,N] split and transposed to [N,K], and C zeroed when split-K halves add into it. The grid is
+// cut into consecutive block ranges, one per part. It lets the GEMM launch at once (the GEMM waits
+// for the prologue's completion before it reads the planes).
+struct SplitJob {
+  const float *a;
+  float *a_hi, *a_lo;
+  int64_t a_rows;
+  const float *b;
+  float *b_hi, *b_lo;
+  int64_t b_rows;  // rows of B [N,K] (b_trans 0)
+  int b_trans, nb, n;  // b_trans 1: B [nb][K][N] transposed to [nb][N][ld]
+  int64_t k, ld;       // operand K and the planes' K pitch
+  float *c;            // zeroed when non-null
+  int64_t c_floats;
+  unsigned ax, ay;      // A part: ax x ay blocks
+  unsigned bx, by, bz;  // B part: bx x by (x bz) blocks
+  unsigned cblocks;     // C part
+};
+
+// Row-major [rows, cols] -> [rows, ld] hi / lo (columns cols..ld-1 zero) by the gx x gy blocks of
+// one part: rows walk by, columns bx / threadIdx.x, so no element index is divided; when the rows
+// need no padding (ld == cols) and the source is 16-byte aligned, whole float4s move instead.
+__device__ __forceinline__ void split_rows_part(const float *__restrict__ src, float *__restrict__ hi,
+                                                float *__restrict__ lo, int64_t rows, int64_t cols, int64_t ld,
+                                                unsigned bx, unsigned by, unsigned gx, unsigned gy) {
   if (ld == cols && !(reinterpret_cast<uintptr_t>(src) & 15) && (cols & 3) == 0) {
     const int64_t n4 = rows * cols / 4;
-    const int64_t stride = (int64_t)gridDim.x * gridDim.y * blockDim.x;
-    for (int64_t i = ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const int64_t stride = (int64_t)gx * gy * blockDim.x;
+    for (int64_t i = ((int64_t)by * gx + bx) * blockDim.x + threadIdx.x; i < n4; i += stride) {
       const float4 x = reinterpret_cast<const float4 *>(src)[i];
       const float4 h = make_float4(to_tf32(x.x), to_tf32(x.y), to_tf32(x.z), to_tf32(x.w));
       reinterpret_cast<float4 *>(hi)[i] = h;
@@ -696,8 +720,8 @@ __global__ void split_rows_kernel(const float *__restrict__ src, float *__restri
     }
     return;
   }
-  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)
-    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < ld; c += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t r = by; r < rows; r += gy)
+    for (int64_t c = (int64_t)bx * blockDim.x + threadIdx.x; c < ld; c += (int64_t)gx * blockDim.x) {
       const float x = c < cols ? src[r * cols + c] : 0.0f;
       const float h = to_tf32(x);
       hi[r * ld + c] = h;
@@ -705,36 +729,85 @@ __global__ void split_rows_kernel(const float *__restrict__ src, float *__restri
     }
 }
 
-// The launch shape of split_rows_kernel: about 8 blocks of 256 threads per SM.
-static inline dim3 split_rows_grid(int64_t rows, int64_t ld) {
-  const int64_t gx = (ld + 255) / 256 < 8 ? (ld + 255) / 256 : 8;
-  const int64_t gy = rows < 148 * 8 / gx ? rows : 148 * 8 / gx;
-  return dim3((unsigned)(gx > 0 ? gx : 1), (unsigned)(gy > 0 ? gy : 1));
-}
-
-// [nb][K][N] -> [nb][N][ld] hi / lo, transposing through a 32x33 shared tile.
-__global__ void split_transpose_kernel(const float *__restrict__ src, float *__restrict__ hi, float *__restrict__ lo,
-                                       int K, int N, int ld) {
-  __shared__ float tile[32][33];
-  const int b = blockIdx.z;
-  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-  const float *s = src + (int64_t)b * K * N;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int k = k0 + i, n = n0 + threadIdx.x;
-    tile[i][threadIdx.x] = (k < K && n < N) ? s[(int64_t)k * N + n] : 0.0f;
+// [nb][K][N] -> [nb][N][ld] hi / lo for one 32 x 32 block (bx over N, by over ld, bz the batch),
+// transposing through a 32 x 33 shared tile; 256 threads as 32 x 8.
+__device__ __forceinline__ void split_transpose_part(const float *__restrict__ src, float *__restrict__ hi,
+                                                     float *__restrict__ lo, int K, int N, int ld, unsigned bx,
+                                                     unsigned by, unsigned bz, float (*tile)[33]) {
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int k0 = by * 32, n0 = bx * 32;
+  const float *s = src + (int64_t)bz * K * N;
+  for (int i = ty; i < 32; i += 8) {
+    const int k = k0 + i, n = n0 + tx;
+    tile[i][tx] = (k < K && n < N) ? s[(int64_t)k * N + n] : 0.0f;
   }
   __syncthreads();
-  float *h = hi + (int64_t)b * N * ld;
-  float *l = lo + (int64_t)b * N * ld;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int n = n0 + i, k = k0 + threadIdx.x;
+  float *h = hi + (int64_t)bz * N * ld;
+  float *l = lo + (int64_t)bz * N * ld;
+  for (int i = ty; i < 32; i += 8) {
+    const int n = n0 + i, k = k0 + tx;
     if (n < N && k < ld) {
-      const float x = tile[threadIdx.x][i];
+      const float x = tile[tx][i];
       const float hv = to_tf32(x);
       h[(int64_t)n * ld + k] = hv;
       l[(int64_t)n * ld + k] = to_tf32(x - hv);
     }
   }
+}
+
+__global__ void split_prologue_kernel(const SplitJob j) {
+  __shared__ float tile[32][33];
+  grid_dependents_launch();  // the GEMM may start its set-up now; it waits for this grid's completion
+  unsigned blk = blockIdx.x;
+  const unsigned na = j.ax * j.ay;
+  if (blk < na) {
+    split_rows_part(j.a, j.a_hi, j.a_lo, j.a_rows, j.k, j.ld, blk % j.ax, blk / j.ax, j.ax, j.ay);
+    return;
+  }
+  blk -= na;
+  const unsigned nbk = j.bx * j.by * j.bz;
+  if (blk < nbk) {
+    if (j.b_trans) {
+      const unsigned bx = blk % j.bx, rest = blk / j.bx;
+      split_transpose_part(j.b, j.b_hi, j.b_lo, (int)j.k, j.n, (int)j.ld, bx, rest % j.by, rest / j.by, tile);
+    } else {
+      split_rows_part(j.b, j.b_hi, j.b_lo, j.b_rows, j.k, j.ld, blk % j.bx, blk / j.bx, j.bx, j.by);
+    }
+    return;
+  }
+  blk -= nbk;
+  // C: 16-byte stores (C's base is 16-byte aligned: it is written through TMA), a scalar tail
+  const int64_t n4 = j.c_floats / 4;
+  const int64_t stride = (int64_t)j.cblocks * blockDim.x;
+  for (int64_t i = (int64_t)blk * blockDim.x + threadIdx.x; i < n4; i += stride)
+    reinterpret_cast<float4 *>(j.c)[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int64_t i = 4 * n4 + (int64_t)blk * blockDim.x + threadIdx.x; i < j.c_floats; i += stride) j.c[i] = 0.0f;
+}
+
+// Fills the block ranges of a SplitJob (about 8 blocks of 256 threads per SM for each row-split
+// part, one per 32 x 32 block for the transpose, up to 4 per SM for C) and launches it.
+static int launch_split_prologue(mpc_device *dev, SplitJob j, cudaStream_t st) {
+  const int64_t sms = dev->prop.multiProcessorCount;
+  auto rows_grid = [sms](int64_t rows, int64_t ld, unsigned &gx, unsigned &gy) {
+    const int64_t x = (ld + 255) / 256 < 8 ? (ld + 255) / 256 : 8;
+    const int64_t y = rows < sms * 8 / x ? rows : sms * 8 / x;
+    gx = (unsigned)(x > 0 ? x : 1);
+    gy = (unsigned)(y > 0 ? y : 1);
+  };
+  rows_grid(j.a_rows, j.ld, j.ax, j.ay);
+  if (j.b_trans) {
+    j.bx = (unsigned)((j.n + 31) / 32), j.by = (unsigned)((j.ld + 31) / 32), j.bz = (unsigned)j.nb;
+  } else {
+    rows_grid(j.b_rows, j.ld, j.bx, j.by);
+    j.bz = 1;
+  }
+  const int64_t cb = (j.c_floats / 4 + 255) / 256;
+  j.cblocks = j.c ? (unsigned)(cb < sms * 4 ? (cb > 0 ? cb : 1) : sms * 4) : 0;
+  const uint64_t total = (uint64_t)j.ax * j.ay + (uint64_t)j.bx * j.by * j.bz + j.cblocks;
+  if (total >= (1ull << 31)) return fail(MPC_ERR_UNSUPPORTED, "gemm: tf32 split prologue of %llu blocks", (unsigned long long)total);
+  split_prologue_kernel<<<(unsigned)total, 256, 0, st>>>(j);
+  dev->launches++;
+  return check_launch(dev, "split_prologue_kernel");
 }
 
 // K == 0: C = epilogue(0).
@@ -786,6 +859,21 @@ int launch(mpc_device *dev, const MapsT<NDST> &maps, const Params &p, cudaStream
     }
     const int pairs = p.tiles_total < pairs_resident[ord] ? p.tiles_total : pairs_resident[ord];
     cfg.gridDim = dim3(2 * pairs);
+    MPC_CUDA(dev, cudaLaunchKernelEx(&cfg, kern, maps, p));
+  } else if constexpr (KIND == kTF32x3) {
+    // Launched programmatically after the split prologue: the set-up (barriers, tensor memory,
+    // descriptor prefetch) overlaps the prologue's last blocks; the kernel waits for its planes.
+    const int grid = p.tiles_total < dev->prop.multiProcessorCount ? p.tiles_total : dev->prop.multiProcessorCount;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     MPC_CUDA(dev, cudaLaunchKernelEx(&cfg, kern, maps, p));
   } else {
     const int grid = p.tiles_total < dev->prop.multiProcessorCount ? p.tiles_total : dev->prop.multiProcessorCount;
@@ -905,10 +993,12 @@ struct OperandScratch {
   Scratch a, b, a2, b2;
 };
 
-// Builds the A / B maps (and runs the tf32 split prologue or the padding copies they need).
+// Builds the A / B maps (and runs the tf32 split prologue or the padding copies they need). c_zero:
+// C, for the split prologue to zero (split-K halves add into it), or null.
 template <int NDST>
 static int operand_maps(mpc_device *dev, const mpc_gemm_desc *d, const Prep &pr, const void *A, const void *B,
-                        MapsT<NDST> &maps, OperandScratch &s, cudaStream_t st) {
+                        MapsT<NDST> &maps, OperandScratch &s, cudaStream_t st, float *c_zero = nullptr,
+                        int64_t c_floats = 0) {
   const int64_t M = d->m, N = d->n, K = d->k, nA = pr.nA, nB = pr.nB;
   const CUtensorMapSwizzle SW = CU_TENSOR_MAP_SWIZZLE_128B;
   int rc;
@@ -917,19 +1007,12 @@ static int operand_maps(mpc_device *dev, const mpc_gemm_desc *d, const Prep &pr,
     if ((rc = s.a.get(dev, st, (size_t)(nA * M * ldk) * 4)) || (rc = s.a2.get(dev, st, (size_t)(nA * M * ldk) * 4)) ||
         (rc = s.b.get(dev, st, (size_t)(nB * N * ldk) * 4)) || (rc = s.b2.get(dev, st, (size_t)(nB * N * ldk) * 4)))
       return rc;
-    split_rows_kernel<<<split_rows_grid(nA * M, ldk), 256, 0, st>>>(static_cast<const float *>(A), (float *)s.a.ptr, (float *)s.a2.ptr,
-                                            nA * M, K, ldk);
-    dev->launches++;
-    if (d->b_layout == MPC_B_NK) {
-      split_rows_kernel<<<split_rows_grid(nB * N, ldk), 256, 0, st>>>(static_cast<const float *>(B), (float *)s.b.ptr, (float *)s.b2.ptr,
-                                              nB * N, K, ldk);
-    } else {
-      dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)nB);
-      split_transpose_kernel<<<g, dim3(32, 8), 0, st>>>(static_cast<const float *>(B), (float *)s.b.ptr,
-                                                         (float *)s.b2.ptr, (int)K, (int)N, (int)ldk);
-    }
-    dev->launches++;
-    if ((rc = check_launch(dev, "split_tf32"))) return rc;
+    SplitJob j = {};
+    j.a = static_cast<const float *>(A), j.a_hi = (float *)s.a.ptr, j.a_lo = (float *)s.a2.ptr, j.a_rows = nA * M;
+    j.b = static_cast<const float *>(B), j.b_hi = (float *)s.b.ptr, j.b_lo = (float *)s.b2.ptr, j.b_rows = nB * N;
+    j.b_trans = d->b_layout == MPC_B_NK ? 0 : 1, j.nb = (int)nB, j.n = (int)N, j.k = K, j.ld = ldk;
+    j.c = c_zero, j.c_floats = c_zero ? c_floats : 0;
+    if ((rc = launch_split_prologue(dev, j, st))) return rc;
     const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     if ((rc = make_map_3d(&maps.a, f32, s.a.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
         (rc = make_map_3d(&maps.a_lo, f32, s.a2.ptr, K, M, nA, ldk * 4, M * ldk * 4, 32, 128, SW)) ||
@@ -1012,8 +1095,10 @@ int gemm_run(mpc_device *dev, const mpc_gemm_desc *d, const void *A, const void 
   if ((rc = make_map_3d(&maps.c[0], tmap_dtype(d->dtype_out), cdst, N, M, batch, ldc * eo, M * ldc * eo,
                         128 / (uint32_t)eo, 32, CU_TENSOR_MAP_SWIZZLE_128B)))
     return rc;
-  if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st))) return rc;
-  if (pr.splits > 1) MPC_CUDA(dev, cudaMemsetAsync(Cout, 0, (size_t)(batch * M * N) * 4, st));  // K halves add into it
+  // split K: the two halves of each tile add into C, which the split prologue zeroes
+  if ((rc = operand_maps(dev, d, pr, A, B, maps, s, st, pr.splits > 1 ? static_cast<float *>(Cout) : nullptr,
+                         batch * M * N)))
+    return rc;
   const bool res16 = (p.epilogue & MPC_EPI_RESIDUAL) && !(p.epilogue & MPC_EPI_GELU) && eo == 2 && p.resid_vec;
   if (pr.tf32 && pr.BN == 64)
     rc = launch<kTF32x3, false, 64, 4>(dev, maps, p, st);
@@ -1200,14 +1285,13 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
   float *b_hi = reinterpret_cast<float *>(scratch + 2 * a_plane);
   float *b_lo = reinterpret_cast<float *>(scratch + 2 * a_plane + b_plane);
   float *cdst = stage_c ? reinterpret_cast<float *>(scratch + 2 * a_plane + 2 * b_plane) : Cout;
-  split_rows_kernel<<<split_rows_grid(pr.nA * M, ldk), 256, 0, st>>>(A, a_hi, a_lo, pr.nA * M, K, ldk);
-  if (d->b_layout == MPC_B_NK) {
-    split_rows_kernel<<<split_rows_grid(pr.nB * N, ldk), 256, 0, st>>>(B, b_hi, b_lo, pr.nB * N, K, ldk);
-  } else {
-    dim3 g((unsigned)((N + 31) / 32), (unsigned)((ldk + 31) / 32), (unsigned)pr.nB);
-    split_transpose_kernel<<<g, dim3(32, 8), 0, st>>>(B, b_hi, b_lo, (int)K, (int)N, (int)ldk);
-  }
-  if ((rc = check_launch(dev, "split_tf32"))) return rc;
+  SplitJob j = {};
+  j.a = A, j.a_hi = a_hi, j.a_lo = a_lo, j.a_rows = pr.nA * M;
+  j.b = B, j.b_hi = b_hi, j.b_lo = b_lo, j.b_rows = pr.nB * N;
+  j.b_trans = d->b_layout == MPC_B_NK ? 0 : 1, j.nb = (int)pr.nB, j.n = (int)N, j.k = K, j.ld = ldk;
+  j.c = pr.splits > 1 ? cdst : nullptr;  // the two K halves of each tile add into it
+  j.c_floats = batch * M * ldc;
+  if ((rc = launch_split_prologue(dev, j, st))) return rc;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
   const CUtensorMapDataType f32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -1218,8 +1302,6 @@ extern "C" int mpc_gemm_f32_noalloc(const mpc_gemm_desc *d, const float *A, cons
       (rc = make_map_3d(&maps.b_lo, f32, b_lo, K, N, pr.nB, ldk * 4, N * ldk * 4, 32, pr.BN, SW)) ||
       (rc = make_map_3d(&maps.c[0], f32, cdst, N, M, batch, ldc * 4, M * ldc * 4, 32, 32, SW)))
     return rc;
-  if (pr.splits > 1)  // the two K halves of each tile add into it
-    MPC_CUDA(dev, cudaMemsetAsync(cdst, 0, (size_t)(batch * M * ldc) * 4, st));
   rc = pr.BN == 64 ? launch<kTF32x3, false, 64, 4>(dev, maps, p, st) : launch<kTF32x3, false, 128, 3>(dev, maps, p, st);
   if (rc) return rc;
   if (stage_c)

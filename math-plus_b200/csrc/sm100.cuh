@@ -139,6 +139,11 @@ template <int N>
 __device__ __forceinline__ void tma_store_wait_all() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
+// Programmatic dependent launch: a kernel launched with programmatic stream serialisation may start
+// while the kernel before it in the stream still runs; griddepcontrol.wait blocks until that kernel
+// has completed and its memory operations are visible, launch_dependents lets the next kernel start.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
