@@ -452,7 +452,7 @@ def setup_gemm(w, dev, torch, g, local, F):
 
     kernel = ("gemm_kernel<kHalf, B MN-major, 256 x 256 tiles on CTA pairs (cta_group::2), 6 stages, 10 warps>"
               if w["dtype"] != "f32"
-              else "gemm_kernel<kTF32x3, BN=128, 3 stages> (+ tf32 split prologue)")
+              else "gemm_kernel<kTF32x3, BN=128, 3 stages>, K split in two halves (+ one split_prologue_kernel launch: A / B hi-lo planes and the zeroing of C; the GEMM launched programmatically after it)")
     return ins, out, launch, kernel
 
 

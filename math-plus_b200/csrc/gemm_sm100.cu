@@ -729,34 +729,53 @@ __device__ __forceinline__ void split_rows_part(const float *__restrict__ src, f
     }
 }
 
-// [nb][K][N] -> [nb][N][ld] hi / lo for one 32 x 32 block (bx over N, by over ld, bz the batch),
-// transposing through a 32 x 33 shared tile; 256 threads as 32 x 8.
+// [nb][K][N] -> [nb][N][ld] hi / lo for one block of 32 K rows x 128 N columns (bx over N, by over
+// ld, bz the batch), transposing through a 32 x 129 shared tile; 256 threads. Loads are float4 along
+// N when B allows it (16-byte base, N a multiple of 4); each warp then writes 16 output rows, lane =
+// k, so every store is one 128-byte row segment and the tile reads are conflict-free.
 __device__ __forceinline__ void split_transpose_part(const float *__restrict__ src, float *__restrict__ hi,
                                                      float *__restrict__ lo, int K, int N, int ld, unsigned bx,
-                                                     unsigned by, unsigned bz, float (*tile)[33]) {
+                                                     unsigned by, unsigned bz, float (*tile)[129]) {
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int k0 = by * 32, n0 = bx * 32;
+  const int k0 = by * 32, n0 = bx * 128;
   const float *s = src + (int64_t)bz * K * N;
-  for (int i = ty; i < 32; i += 8) {
-    const int k = k0 + i, n = n0 + tx;
-    tile[i][tx] = (k < K && n < N) ? s[(int64_t)k * N + n] : 0.0f;
+  const bool vec = !(reinterpret_cast<uintptr_t>(src) & 15) && (N & 3) == 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int kr = ty + 8 * i, k = k0 + kr, n = n0 + 4 * tx;
+    float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (k < K) {
+      if (vec && n + 3 < N) {
+        x = *reinterpret_cast<const float4 *>(s + (int64_t)k * N + n);
+      } else {
+        const float *row = s + (int64_t)k * N;
+        if (n < N) x.x = row[n];
+        if (n + 1 < N) x.y = row[n + 1];
+        if (n + 2 < N) x.z = row[n + 2];
+        if (n + 3 < N) x.w = row[n + 3];
+      }
+    }
+    tile[kr][4 * tx] = x.x, tile[kr][4 * tx + 1] = x.y, tile[kr][4 * tx + 2] = x.z, tile[kr][4 * tx + 3] = x.w;
   }
   __syncthreads();
-  float *h = hi + (int64_t)bz * N * ld;
-  float *l = lo + (int64_t)bz * N * ld;
-  for (int i = ty; i < 32; i += 8) {
-    const int n = n0 + i, k = k0 + tx;
-    if (n < N && k < ld) {
-      const float x = tile[tx][i];
+  const int k = k0 + tx;
+  if (k >= ld) return;
+  float *h = hi + (int64_t)bz * N * ld + k;
+  float *l = lo + (int64_t)bz * N * ld + k;
+#pragma unroll 4
+  for (int r = 0; r < 16; ++r) {
+    const int nl = ty * 16 + r, n = n0 + nl;
+    if (n < N) {
+      const float x = tile[tx][nl];
       const float hv = to_tf32(x);
-      h[(int64_t)n * ld + k] = hv;
-      l[(int64_t)n * ld + k] = to_tf32(x - hv);
+      h[(int64_t)n * ld] = hv;
+      l[(int64_t)n * ld] = to_tf32(x - hv);
     }
   }
 }
 
 __global__ void split_prologue_kernel(const SplitJob j) {
-  __shared__ float tile[32][33];
+  __shared__ float tile[32][129];
   grid_dependents_launch();  // the GEMM may start its set-up now; it waits for this grid's completion
   unsigned blk = blockIdx.x;
   const unsigned na = j.ax * j.ay;
@@ -784,25 +803,32 @@ __global__ void split_prologue_kernel(const SplitJob j) {
   for (int64_t i = 4 * n4 + (int64_t)blk * blockDim.x + threadIdx.x; i < j.c_floats; i += stride) j.c[i] = 0.0f;
 }
 
-// Fills the block ranges of a SplitJob (about 8 blocks of 256 threads per SM for each row-split
-// part, one per 32 x 32 block for the transpose, up to 4 per SM for C) and launches it.
+// Fills the block ranges of a SplitJob and launches it: a row split moves about four float4s per
+// thread when its rows are contiguous (else up to 8 blocks per SM walk the rows), the transpose takes
+// one block per 32 x 128 tile, the zeroing of C about four float4s per thread; for 1024^3 the whole
+// prologue is one wave of blocks.
 static int launch_split_prologue(mpc_device *dev, SplitJob j, cudaStream_t st) {
   const int64_t sms = dev->prop.multiProcessorCount;
-  auto rows_grid = [sms](int64_t rows, int64_t ld, unsigned &gx, unsigned &gy) {
+  auto clamp_blocks = [sms](int64_t b) { return (unsigned)(b < 1 ? 1 : b < sms * 8 ? b : sms * 8); };
+  auto rows_grid = [&](const float *src, int64_t rows, int64_t ld, unsigned &gx, unsigned &gy) {
+    if (ld == j.k && !(reinterpret_cast<uintptr_t>(src) & 15) && (j.k & 3) == 0) {  // the flat float4 path
+      gx = 1;
+      gy = clamp_blocks((rows * ld / 4 + 1023) / 1024);
+      return;
+    }
     const int64_t x = (ld + 255) / 256 < 8 ? (ld + 255) / 256 : 8;
     const int64_t y = rows < sms * 8 / x ? rows : sms * 8 / x;
     gx = (unsigned)(x > 0 ? x : 1);
     gy = (unsigned)(y > 0 ? y : 1);
   };
-  rows_grid(j.a_rows, j.ld, j.ax, j.ay);
+  rows_grid(j.a, j.a_rows, j.ld, j.ax, j.ay);
   if (j.b_trans) {
-    j.bx = (unsigned)((j.n + 31) / 32), j.by = (unsigned)((j.ld + 31) / 32), j.bz = (unsigned)j.nb;
+    j.bx = (unsigned)((j.n + 127) / 128), j.by = (unsigned)((j.ld + 31) / 32), j.bz = (unsigned)j.nb;
   } else {
-    rows_grid(j.b_rows, j.ld, j.bx, j.by);
+    rows_grid(j.b, j.b_rows, j.ld, j.bx, j.by);
     j.bz = 1;
   }
-  const int64_t cb = (j.c_floats / 4 + 255) / 256;
-  j.cblocks = j.c ? (unsigned)(cb < sms * 4 ? (cb > 0 ? cb : 1) : sms * 4) : 0;
+  j.cblocks = j.c ? clamp_blocks((j.c_floats / 4 + 1023) / 1024) : 0;
   const uint64_t total = (uint64_t)j.ax * j.ay + (uint64_t)j.bx * j.by * j.bz + j.cblocks;
   if (total >= (1ull << 31)) return fail(MPC_ERR_UNSUPPORTED, "gemm: tf32 split prologue of %llu blocks", (unsigned long long)total);
   split_prologue_kernel<<<(unsigned)total, 256, 0, st>>>(j);
