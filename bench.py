@@ -553,6 +553,19 @@ def time_region(dev, stream, fn, steps, barrier):
     return dev.elapsed_ms(e0, e1) / steps
 
 
+def host_link_floor_ms(h2d_bytes, d2h_bytes, bw):
+    """Least time per step for the streamed e2e leg's copies: a step's uploads and the previous
+    step's read-back run at once at the rates measured for both directions together until the
+    smaller transfer is done; the rest of the larger one then moves at its rate alone."""
+    th = h2d_bytes / (bw["bidir_h2d_gbs"] * 1e9)
+    td = d2h_bytes / (bw["bidir_d2h_gbs"] * 1e9)
+    if th <= td:
+        rest = d2h_bytes - th * bw["bidir_d2h_gbs"] * 1e9
+        return (th + rest / (bw["d2h_gbs"] * 1e9)) * 1e3
+    rest = h2d_bytes - td * bw["bidir_h2d_gbs"] * 1e9
+    return (td + rest / (bw["h2d_gbs"] * 1e9)) * 1e3
+
+
 def pinned_copy_gbs(dev, nbytes=256 << 20, reps=5):
     """Host<->device copy bandwidth from pinned memory (GB/s), CUDA events: each direction alone, and
     both at once on two streams (the end-to-end leg overlaps them): the roofline of its transfers."""
@@ -768,10 +781,10 @@ def measure_workload(args, w, name, ctx):
             # read-back of the previous step overlaps them on the other copy engine)
             bw = pinned_copy_gbs(dev)
             h2d_b, d2h_b = e2e["h2d_bytes_per_step"], e2e["d2h_bytes_per_step"]
-            # both directions move at once in the streamed leg: the floor uses their concurrent rates
-            floor_ms = max(h2d_b / (bw["bidir_h2d_gbs"] * 1e9), d2h_b / (bw["bidir_d2h_gbs"] * 1e9)) * 1e3
+            floor_ms = host_link_floor_ms(h2d_b, d2h_b, bw)
             e2e["host_link"] = dict(bw, source="measured: 256 MiB pinned copies, CUDA events, this box; the floor "
-                                               "uses the rates of both directions at once",
+                                               "moves both directions at their concurrent rates until the smaller "
+                                               "is done, then the rest of the larger at its rate alone",
                                     floor_ms_per_step=floor_ms, frac_of_floor=floor_ms / e2e["ms_per_step"])
 
     if extras:

@@ -39,3 +39,18 @@ def test_reference_arm_line(extra):
         assert att["impl"] == "reference" and att["unit"] == "TFLOP/s"
     if "--precision" in extra:
         assert "gelu" in d["metric"] and "f32 evaluation" in d["metric"] and d["dtype"] == "f32"
+
+
+def test_host_link_floor():
+    """The e2e leg's copy floor: equal transfers take the concurrent rate throughout; for unequal
+    ones the rest of the larger transfer moves at its rate alone once the smaller is done."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", os.path.join(ROOT, "bench.py"))
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    bw = dict(h2d_gbs=50.0, d2h_gbs=60.0, bidir_h2d_gbs=40.0, bidir_d2h_gbs=40.0)
+    assert b.host_link_floor_ms(40e9, 40e9, bw) == pytest.approx(1000.0)
+    # 1 s together moves 40 GB each way; the remaining 20 GB of uploads take 0.4 s alone
+    assert b.host_link_floor_ms(60e9, 40e9, bw) == pytest.approx(1400.0)
+    assert b.host_link_floor_ms(40e9, 100e9, bw) == pytest.approx(2000.0)
+    assert b.host_link_floor_ms(40e9, 0, bw) == pytest.approx(800.0)
