@@ -133,9 +133,9 @@ def test_differential_sdpa_cases(dev, golden_dir):
                                          # pairs; the last q-block of each head has no second tile
 ])
 def test_tensor_core_path_shapes(dev, dtype, B, H, Hk, Lq, Lk, D, causal):
-    """Every causal case here has fewer heavy / light unit pairs than a whole number of rounds over
-    the SMs, so the host deals its units in the cost-sorted snake order; the non-causal cases and
-    the full causal configuration (test_causal_attention_full_config_sampled) take the pairs."""
+    """For every causal case here the heavy / light unit pairs leave CTAs unevenly loaded, so the
+    host deals the units in the cost-sorted snake order instead; the non-causal cases and the full
+    causal configuration (test_causal_attention_full_config_sampled) take the pairs."""
     q = exact(O.normal_f32(B * H * Lq * D, 31).reshape(B, H, Lq, D), dtype)
     k = exact(O.normal_f32(B * Hk * Lk * D, 32).reshape(B, Hk, Lk, D), dtype)
     v = exact(O.normal_f32(B * Hk * Lk * D, 33).reshape(B, Hk, Lk, D), dtype)
