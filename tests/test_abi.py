@@ -100,3 +100,23 @@ def test_missing_library_raises_instead_of_falling_back(tmp_path):
     from tensor_cuda import _ffi as F
     with pytest.raises(OSError, match="not found"):
         F.load(str(tmp_path / "nope.so"))
+
+
+def test_typescript_symbol_tables_cover_the_header():
+    """The Deno.dlopen / bun:ffi tables generated for the TypeScript package name every function
+    of the header with one FFI type per C parameter; descriptor structs and out-parameters are
+    buffers, device pointers and handles opaque pointers, the waits nonblocking."""
+    from tensor_cuda import ts_symbols as T
+    deno, bun = T.table(), T.table(bun=True)
+    assert sorted(deno) == declared_functions() == sorted(bun)
+    assert deno["mpc_gemm"] == {"parameters": ["pointer", "buffer", "pointer", "pointer", "pointer", "pointer",
+                                                "pointer"], "result": "i32"}
+    assert deno["mpc_device_create"]["parameters"] == ["i32", "u32", "buffer"]
+    assert deno["mpc_alloc"]["parameters"] == ["pointer", "usize", "buffer"]
+    assert deno["mpc_layer_norm"]["parameters"][5] == "f32" and deno["mpc_rope"]["parameters"][7] == "f64"
+    assert deno["mpc_stream_sync"].get("nonblocking") and deno["mpc_sync"].get("nonblocking")
+    assert deno["mpc_last_error"]["result"] == "pointer" and bun["mpc_last_error"]["returns"] == "ptr"
+    assert bun["mpc_gemm"]["args"][1] == "ptr" and bun["mpc_alloc"]["args"][1] == "u64"
+    src = T.render()
+    assert src.count("parameters:") == len(deno) and src.count("{") == src.count("}")
+    assert T.render(bun=True).count("FFIType.i32") >= len(bun)
