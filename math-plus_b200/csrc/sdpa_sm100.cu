@@ -157,13 +157,18 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Head dim 64 issues each Q tile's MMAs from its own thread (warps 9 and 10), so that one tile's
+  // QK and PV follow its own softmax instead of waiting in one in-order stream behind the other
+  // tile's; at head dim 128 the single interleaved stream measured faster.
+  constexpr bool kDualIssue = D == 64;
+  constexpr int kIssuers = kDualIssue ? 2 : 1;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    mbar_init(q_empty, kIssuers);
     for (int s = 0; s < C::SLOTS; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], kIssuers);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(&s_ready[t], 1);
@@ -171,7 +176,7 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
       mbar_init(&o_ready[t], 1);
       mbar_init(&o_free[t], 4);
     }
-    mbar_init(drain, 1);
+    mbar_init(drain, kIssuers);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -188,8 +193,8 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
   // gives registers to the two softmax warpgroups, which keep a whole 128-key score row in
   // registers. Launched at 168 per thread (the host checks):
   // 2 x 128 x 208 + 128 x 88 = 64512 = 384 x 168.
-  if (warp >= 10) {
-    reg_dealloc<88>();  // the warpgroup's two spare warps only wait for the end
+  if (warp >= 10 + (kDualIssue ? 1 : 0)) {
+    reg_dealloc<88>();  // the warpgroup's spare warps only wait for the end
   } else if (warp == 8) {
     reg_dealloc<88>();
     // ---------------- TMA producer ----------------
@@ -229,84 +234,152 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
           mbar_wait(&kv_full[i % C::SLOTS], (i / C::SLOTS) & 1, &never, p.err, kErrWaitProducer, p.timeout_ns);
       }
     }
-  } else if (warp == 9) {
-    // ---------------- MMA issuer ----------------
-    reg_dealloc<88>();
-    if (lane == 0) {
-      const uint32_t q_addr = smem_u32(sq);
-      auto qk = [&](int t, int slot) {
-        const uint32_t a0 = q_addr + t * C::TILE, b0 = smem_u32(skv + slot * C::TILE);
+  } else if (warp == 9 || (kDualIssue && warp == 10)) {
+    if constexpr (kDualIssue) {
+      // ---------------- MMA issuers: warp 9 for Q tile 0, warp 10 for Q tile 1 ----------------
+      reg_dealloc<88>();
+      if (lane == 0) {
+        const int t = warp - 9;
+        const uint32_t q_addr = smem_u32(sq) + t * C::TILE;
+        auto qk = [&](int slot) {
+          const uint32_t b0 = smem_u32(skv + slot * C::TILE);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * C::SUB + (kk & 3) * 32;
-          mma_f16_ss(tmem + t * 128, make_sdesc(a0 + off, 16, 1024), make_sdesc(b0 + off, 16, 1024), p.idesc_qk,
-                     kk ? 1u : 0u);
-        }
-      };
-      auto pv = [&](int t, int slot, bool first) {
-        const uint32_t v0 = smem_u32(skv + slot * C::TILE);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per MMA; P packs 2 keys per TMEM column
-          mma_f16_ts(tmem + 256 + t * D, tmem + t * 128 + kk * 8, make_sdesc(v0 + kk * 2048, C::SUB, 1024),
-                     p.idesc_pv, (first && kk == 0) ? 0u : 1u);
-      };
-      int ring = 0;                 // K/V ring items consumed so far (K_j, V_j of every unit in order)
-      int pv_cnt0 = 0, pv_cnt1 = 0;  // PV products issued per Q tile (p_ready phases)
-      bool ok = true;
-      auto wait_item = [&](int i) {
-        return mbar_wait(&kv_full[i % C::SLOTS], (i / C::SLOTS) & 1, abort_flag, p.err, kErrWaitConsumer,
-                         p.timeout_ns);
-      };
-      Unit w;
-      for (int k = 0; ok && unit_of<SNAKE>(p, k, w); ++k) {
-        auto need = [&](int t, int j) { return j <= (t ? w.last1 : w.last0); };
-        const int base = ring;  // K_j is ring item base + 2j, V_j item base + 2j + 1
-        auto do_pv = [&](int t, int j, int sv, int &cnt) -> bool {
-          if (j == 0 && k > 0) {  // O_t still holds the previous unit until its output has been read
-            if (!mbar_wait(&o_free[t], (k - 1) & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns)) return false;
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * C::SUB + (kk & 3) * 32;
+            mma_f16_ss(tmem + t * 128, make_sdesc(q_addr + off, 16, 1024), make_sdesc(b0 + off, 16, 1024), p.idesc_qk,
+                       kk ? 1u : 0u);
           }
-          if (!mbar_wait(&p_ready[t], cnt & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns)) return false;
-          tc_fence_after();
-          pv(t, sv, j == 0);
-          tc_commit(&o_ready[t]);
-          ++cnt;
-          return true;
         };
-        if (!(ok = mbar_wait(q_full, k & 1, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns))) break;
-        if (!(ok = wait_item(base))) break;
-        tc_fence_after();
-        if (need(0, 0)) {
-          qk(0, base % C::SLOTS);
-          tc_commit(&s_ready[0]);
-        }
-        for (int j = 0; j < w.n_kv; ++j) {
-          const int sk = (base + 2 * j) % C::SLOTS, sv = (base + 2 * j + 1) % C::SLOTS;
-          if (need(1, j)) {
-            qk(1, sk);
-            tc_commit(&s_ready[1]);
-          }
-          // K_j is consumed once both QK products have run; after the last QK, so is Q.
-          tc_commit(&kv_empty[sk]);
-          if (j + 1 == w.n_kv) tc_commit(q_empty);
-          if (!(ok = wait_item(base + 2 * j + 1))) break;
-          tc_fence_after();
-          if (need(0, j) && !(ok = do_pv(0, j, sv, pv_cnt0))) break;
-          if (j + 1 < w.n_kv) {
-            if (!(ok = wait_item(base + 2 * (j + 1)))) break;
+        auto pv = [&](int slot, bool first) {
+          const uint32_t v0 = smem_u32(skv + slot * C::TILE);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per MMA; P packs 2 keys per TMEM column
+            mma_f16_ts(tmem + 256 + t * D, tmem + t * 128 + kk * 8, make_sdesc(v0 + kk * 2048, C::SUB, 1024),
+                       p.idesc_pv, (first && kk == 0) ? 0u : 1u);
+        };
+        int ring = 0;    // K/V ring items consumed so far (K_j, V_j of every unit in order)
+        int pv_cnt = 0;  // PV products issued for this tile (p_ready phases)
+        bool ok = true;
+        auto wait_item = [&](int i) {
+          return mbar_wait(&kv_full[i % C::SLOTS], (i / C::SLOTS) & 1, abort_flag, p.err, kErrWaitConsumer,
+                           p.timeout_ns);
+        };
+        Unit w;
+        for (int k = 0; ok && unit_of<SNAKE>(p, k, w); ++k) {
+          const int last = t ? w.last1 : w.last0;  // -1 for a missing second tile
+          const int base = ring;                   // K_j is ring item base + 2j, V_j item base + 2j + 1
+          if (!(ok = mbar_wait(q_full, k & 1, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns))) break;
+          for (int j = 0; j < w.n_kv; ++j) {
+            const int sk = (base + 2 * j) % C::SLOTS, sv = (base + 2 * j + 1) % C::SLOTS;
+            const bool need = j <= last;
+            // Every ring item is waited for before it is released, so a release always counts toward
+            // the item's own round of the slot (the producer reloads it only after both releases).
+            if (!(ok = wait_item(base + 2 * j))) break;
             tc_fence_after();
-            if (need(0, j + 1)) {
-              qk(0, (base + 2 * (j + 1)) % C::SLOTS);
-              tc_commit(&s_ready[0]);
+            if (need) {
+              qk(sk);
+              tc_commit(&s_ready[t]);
             }
+            tc_commit(&kv_empty[sk]);                 // K_j: once this tile's QK has read it
+            if (j + 1 == w.n_kv) tc_commit(q_empty);  // Q: once this tile's last QK has run
+            if (!(ok = wait_item(base + 2 * j + 1))) break;
+            if (need) {
+              if (j == 0 && k > 0) {  // O_t still holds the previous unit until its output has been read
+                if (!(ok = mbar_wait(&o_free[t], (k - 1) & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
+              }
+              if (!(ok = mbar_wait(&p_ready[t], pv_cnt & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns))) break;
+              tc_fence_after();
+              pv(sv, j == 0);
+              tc_commit(&o_ready[t]);
+              ++pv_cnt;
+            }
+            tc_commit(&kv_empty[sv]);  // V_j: once this tile's PV has read it
           }
-          if (need(1, j) && !(ok = do_pv(1, j, sv, pv_cnt1))) break;
-          tc_commit(&kv_empty[sv]);
+          ring = base + 2 * w.n_kv;
         }
-        ring = base + 2 * w.n_kv;
+        tc_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never, p.err, kErrWaitConsumer, p.timeout_ns);
       }
-      tc_commit(drain);
-      volatile int never = 0;
-      mbar_wait(drain, 0, &never, p.err, kErrWaitConsumer, p.timeout_ns);
+    } else {
+      // ---------------- MMA issuer ----------------
+      reg_dealloc<88>();
+      if (lane == 0) {
+        const uint32_t q_addr = smem_u32(sq);
+        auto qk = [&](int t, int slot) {
+          const uint32_t a0 = q_addr + t * C::TILE, b0 = smem_u32(skv + slot * C::TILE);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * C::SUB + (kk & 3) * 32;
+            mma_f16_ss(tmem + t * 128, make_sdesc(a0 + off, 16, 1024), make_sdesc(b0 + off, 16, 1024), p.idesc_qk,
+                       kk ? 1u : 0u);
+          }
+        };
+        auto pv = [&](int t, int slot, bool first) {
+          const uint32_t v0 = smem_u32(skv + slot * C::TILE);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per MMA; P packs 2 keys per TMEM column
+            mma_f16_ts(tmem + 256 + t * D, tmem + t * 128 + kk * 8, make_sdesc(v0 + kk * 2048, C::SUB, 1024),
+                       p.idesc_pv, (first && kk == 0) ? 0u : 1u);
+        };
+        int ring = 0;                 // K/V ring items consumed so far (K_j, V_j of every unit in order)
+        int pv_cnt0 = 0, pv_cnt1 = 0;  // PV products issued per Q tile (p_ready phases)
+        bool ok = true;
+        auto wait_item = [&](int i) {
+          return mbar_wait(&kv_full[i % C::SLOTS], (i / C::SLOTS) & 1, abort_flag, p.err, kErrWaitConsumer,
+                           p.timeout_ns);
+        };
+        Unit w;
+        for (int k = 0; ok && unit_of<SNAKE>(p, k, w); ++k) {
+          auto need = [&](int t, int j) { return j <= (t ? w.last1 : w.last0); };
+          const int base = ring;  // K_j is ring item base + 2j, V_j item base + 2j + 1
+          auto do_pv = [&](int t, int j, int sv, int &cnt) -> bool {
+            if (j == 0 && k > 0) {  // O_t still holds the previous unit until its output has been read
+              if (!mbar_wait(&o_free[t], (k - 1) & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns)) return false;
+            }
+            if (!mbar_wait(&p_ready[t], cnt & 1, abort_flag, p.err, kErrWaitSoftmax, p.timeout_ns)) return false;
+            tc_fence_after();
+            pv(t, sv, j == 0);
+            tc_commit(&o_ready[t]);
+            ++cnt;
+            return true;
+          };
+          if (!(ok = mbar_wait(q_full, k & 1, abort_flag, p.err, kErrWaitConsumer, p.timeout_ns))) break;
+          if (!(ok = wait_item(base))) break;
+          tc_fence_after();
+          if (need(0, 0)) {
+            qk(0, base % C::SLOTS);
+            tc_commit(&s_ready[0]);
+          }
+          for (int j = 0; j < w.n_kv; ++j) {
+            const int sk = (base + 2 * j) % C::SLOTS, sv = (base + 2 * j + 1) % C::SLOTS;
+            if (need(1, j)) {
+              qk(1, sk);
+              tc_commit(&s_ready[1]);
+            }
+            // K_j is consumed once both QK products have run; after the last QK, so is Q.
+            tc_commit(&kv_empty[sk]);
+            if (j + 1 == w.n_kv) tc_commit(q_empty);
+            if (!(ok = wait_item(base + 2 * j + 1))) break;
+            tc_fence_after();
+            if (need(0, j) && !(ok = do_pv(0, j, sv, pv_cnt0))) break;
+            if (j + 1 < w.n_kv) {
+              if (!(ok = wait_item(base + 2 * (j + 1)))) break;
+              tc_fence_after();
+              if (need(0, j + 1)) {
+                qk(0, (base + 2 * (j + 1)) % C::SLOTS);
+                tc_commit(&s_ready[0]);
+              }
+            }
+            if (need(1, j) && !(ok = do_pv(1, j, sv, pv_cnt1))) break;
+            tc_commit(&kv_empty[sv]);
+          }
+          ring = base + 2 * w.n_kv;
+        }
+        tc_commit(drain);
+        volatile int never = 0;
+        mbar_wait(drain, 0, &never, p.err, kErrWaitConsumer, p.timeout_ns);
+      }
     }
   } else {
     // ---------------- softmax + correction + output (warps 0-7) ----------------
