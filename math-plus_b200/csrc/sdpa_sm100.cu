@@ -137,7 +137,7 @@ __device__ __forceinline__ void load_rows(const CUtensorMap *map, uint64_t *bar,
 
 // BF: bf16 operands (P is packed as bf16), else f16. A template parameter, not a run-time flag, so
 // that the softmax's inner loops carry no per-element branch on the type.
-template <int D, bool BF, bool SNAKE>
+template <int D, bool BF, bool SNAKE, bool DUAL>
 __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Maps maps, const Params p) {
   using C = Cfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -158,10 +158,12 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Head dim 64 issues each Q tile's MMAs from its own thread (warps 9 and 10), so that one tile's
-  // QK and PV follow its own softmax instead of waiting in one in-order stream behind the other
-  // tile's; at head dim 128 the single interleaved stream measured faster.
-  constexpr bool kDualIssue = D == 64;
+  // DUAL: each Q tile's MMAs come from their own thread (warps 9 and 10), so that one tile's QK and
+  // PV follow its own softmax instead of waiting in one in-order stream behind the other tile's,
+  // and a tile that finishes a unit early moves on to the next one. The host picks it for causal
+  // launches over at most 1024 keys, where unit boundaries are frequent; over longer or
+  // non-causal rows the single interleaved stream measured faster.
+  constexpr bool kDualIssue = DUAL;
   constexpr int kIssuers = kDualIssue ? 2 : 1;
 
   if (threadIdx.x == 0) {
@@ -683,36 +685,45 @@ static bool prefer_snake(const Params &p, long long grid_pairs, long long grid_s
   return mb * 100 < ma * 97;
 }
 
-template <int D, bool BF, bool SNAKE>
+template <int D, bool BF, bool SNAKE, bool DUAL>
 int launch_order(mpc_device *dev, const Maps &maps, const Params &p, long long grid, cudaStream_t st) {
   using C = Cfg<D>;
   static bool configured[64] = {};
   const int ord = dev->ordinal & 63;
   if (!configured[ord]) {
-    MPC_CUDA(dev, cudaFuncSetAttribute(attn_kernel<D, BF, SNAKE>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    MPC_CUDA(dev, cudaFuncSetAttribute(attn_kernel<D, BF, SNAKE, DUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     cudaFuncAttributes fa;
-    MPC_CUDA(dev, cudaFuncGetAttributes(&fa, attn_kernel<D, BF, SNAKE>));
+    MPC_CUDA(dev, cudaFuncGetAttributes(&fa, attn_kernel<D, BF, SNAKE, DUAL>));
     // The register split inside the kernel is sized for a 168-register launch; refuse anything else
     // rather than launch a split whose increase could never be granted.
     if (fa.numRegs != 168)
       return fail(MPC_ERR_UNSUPPORTED, "attn_kernel built with %d registers per thread (expected 168)", fa.numRegs);
     configured[ord] = true;
   }
-  attn_kernel<D, BF, SNAKE><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(maps, p);
+  attn_kernel<D, BF, SNAKE, DUAL><<<(unsigned)grid, C::THREADS, C::SMEM, st>>>(maps, p);
   dev->launches++;
   return check_launch(dev, "attn_kernel");
 }
 
-// Persistent: one CTA per SM (at most), each taking units until none is left; the unit order is a
-// separate instantiation so that the pairs' kernel carries no branch for the other order.
+// Persistent: one CTA per SM (at most), each taking units until none is left. The unit order and
+// the MMA issuers are separate instantiations, so that no kernel carries a branch for the others.
+// Measured (causal, A/B on one box each time): [8,16,1024,128] bf16 383-422 TFLOP/s with one
+// issuer per tile against 364-369 with one stream; [16,16,512,128] f16 318 against 292-313;
+// [32,12,1024,64] f16 306-314 against 293-301; [16,32,2048,128] f16 707 against 814 and
+// non-causal rows 756-774 against 873-1009, so those keep the one stream.
 template <int D, bool BF>
 int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
   const long long sms = dev->prop.multiProcessorCount;
   const long long pairs = ((long long)p.n_units + 1) / 2;
   const long long grid = pairs < sms ? pairs : sms;
   const long long grid_snake = p.n_units < sms ? p.n_units : sms;
-  if (p.causal && prefer_snake(p, grid, grid_snake)) return launch_order<D, BF, true>(dev, maps, p, grid_snake, st);
-  return launch_order<D, BF, false>(dev, maps, p, grid, st);
+  if (!p.causal) return launch_order<D, BF, false, false>(dev, maps, p, grid, st);
+  const bool snake = prefer_snake(p, grid, grid_snake);
+  if (p.Lk <= 1024)
+    return snake ? launch_order<D, BF, true, true>(dev, maps, p, grid_snake, st)
+                 : launch_order<D, BF, false, true>(dev, maps, p, grid, st);
+  return snake ? launch_order<D, BF, true, false>(dev, maps, p, grid_snake, st)
+               : launch_order<D, BF, false, false>(dev, maps, p, grid, st);
 }
 
 }  // namespace attn
