@@ -16,9 +16,10 @@
 //                    O_t += P_t·V_j (A = P from TMEM, B = V MN-major); owns the TMEM allocation
 //   warps 10-11      idle (they complete the load / MMA warpgroup for register reconfiguration)
 //   issue order per KV tile j: QK(1,j), PV(0,j), QK(0,j+1), PV(1,j), so each Q tile's softmax runs
-//   while the tensor core works on the other tile. At head dim 64 warp 10 issues Q tile 1's MMAs
-//   and warp 9 only tile 0's, each in its own order QK(t,j), PV(t,j), QK(t,j+1). Causal: KV tiles
-//   past a Q tile's diagonal are skipped, only diagonal tiles are masked element-wise.
+//   while the tensor core works on the other tile. For causal launches over at most 1024 keys
+//   warp 10 issues Q tile 1's MMAs and warp 9 only tile 0's, each in its own order QK(t,j),
+//   PV(t,j), QK(t,j+1). Causal: KV tiles past a Q tile's diagonal are skipped, only diagonal tiles
+//   are masked element-wise.
 //   TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
 // Generic path (any head dim <= 256, f32 / f16 / bf16, any alignment): one warp per query row on the
 // CUDA cores, online softmax in f32 — the role of backend-webgpu's generic sdpa kernel.
