@@ -13,6 +13,8 @@ A step is one pass of the hot path over one batch of synthetic input:
                                (packages/tensor-cpu/src/index.ts:755-762, :598) as one kernel.
   causal_attention_f16         causal sdpa, Q/K/V [16, 32, 2048, 128] f16, scale 1/sqrt(128), f16 out
                                (+ f32 log-sum-exp): Backend.sdpa (index.ts:821-840) as one kernel.
+  gpt2_attention_bf16          the same op at GPT-2-small's attention shape, causal bf16 [32, 12, 1024,
+                               64] (a profiling case for the forward's attention launches).
   gemm_f32_1024                one f32 1024^3 GEMM (3xTF32 on the tensor cores); L2 is flushed
                                between timed steps (the inputs are 8 MiB).
   nsplit_gemm_bf16             C[16384,65536] = A[16384,8192] @ B[8192,65536] bf16 -> bf16 with B's
@@ -76,6 +78,10 @@ WORKLOADS = {
     "causal_attention_f16": dict(kind="attention", batch=16, heads=32, seq=2048, head_dim=128, dtype="f16",
                                  causal=True, metric="fused attention TFLOP/s (causal f16)",
                                  desc="causal sdpa f16 [16,32,2048,128], scale 1/sqrt(128), f16 out + f32 LSE"),
+    "gpt2_attention_bf16": dict(kind="attention", batch=32, heads=12, seq=1024, head_dim=64, dtype="bf16",
+                                causal=True, metric="fused attention TFLOP/s (causal bf16, GPT-2 shape)",
+                                desc="causal sdpa bf16 [32,12,1024,64] (one GPT-2-small layer's attention at "
+                                     "batch 32 x 1024 tokens), scale 1/8, bf16 out + f32 LSE"),
 }
 
 
@@ -460,7 +466,8 @@ def setup_attention(w, dev, torch, g, local, F):
     from tensor_cuda.runtime import sdpa_desc
     B_, H, L, D = w["batch"], w["heads"], w["seq"], w["head_dim"]
     dvc = f"cuda:{local}"
-    q, k, v = (torch.randn((B_, H, L, D), generator=g, device=dvc).half() for _ in range(3))
+    tdt = torch.bfloat16 if w["dtype"] == "bf16" else torch.float16
+    q, k, v = (torch.randn((B_, H, L, D), generator=g, device=dvc).to(tdt) for _ in range(3))
     out = dev.alloc(B_ * H * L * D * 2)
     lse = dev.alloc(B_ * H * L * 4)
     desc = sdpa_desc(B_, H, H, L, L, D, D, F.DTYPE_CODES[w["dtype"]], w["causal"], 1 / math.sqrt(D))
