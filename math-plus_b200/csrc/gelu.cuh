@@ -18,11 +18,12 @@
 namespace mpc {
 namespace gelu_detail {
 
-// P's coefficients, highest degree first, already multiplied by ½.
-#define MPC_GELU_P(X) \
-  X(0.029522638767957687f) X(-0.13134364783763885f) X(0.18237833678722382f) X(-0.081276483833789825f) \
-  X(0.11541666835546494f) X(0.06914050877094269f) X(0.10200400650501251f) X(0.10695201903581619f)   \
-  X(0.10720596462488174f)
+// P's coefficients, highest degree first, already multiplied by ½: the leading one, then the rest
+// (Horner's scheme starts from the leading coefficient, so no multiply-add is spent on a zero).
+#define MPC_GELU_P_LEAD 0.029522638767957687f
+#define MPC_GELU_P_REST(X)                                                                           \
+  X(-0.13134364783763885f) X(0.18237833678722382f) X(-0.081276483833789825f) X(0.11541666835546494f) \
+  X(0.06914050877094269f) X(0.10200400650501251f) X(0.10695201903581619f) X(0.10720596462488174f)
 constexpr float kInvSqrt2 = 0.70710678118654752f;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -68,9 +69,9 @@ __device__ __forceinline__ float gelu_erf_f32(float x) {
   using namespace gelu_detail;
   const float t = fabsf(x) * kInvSqrt2;
   const float u = rcp_approx(fmaf(0.38f, t, 1.0f));
-  float p = 0.0f;
+  float p = MPC_GELU_P_LEAD;
 #define MPC_HORNER(c) p = fmaf(p, u, c);
-  MPC_GELU_P(MPC_HORNER)
+  MPC_GELU_P_REST(MPC_HORNER)
 #undef MPC_HORNER
   const float hi = t * t;
   const float lo = fmaf(t, t, -hi);
@@ -85,9 +86,9 @@ __device__ __forceinline__ void gelu_erf_f32x2(float &x0, float &x1) {
   const unsigned long long t = mul2(pk(fabsf(x0), fabsf(x1)), pk(kInvSqrt2, kInvSqrt2));
   const float2 d = unpk(fma2(pk(0.38f, 0.38f), t, pk(1.0f, 1.0f)));
   const unsigned long long u = pk(rcp_approx(d.x), rcp_approx(d.y));
-  unsigned long long p = pk(0.0f, 0.0f);
+  unsigned long long p = pk(MPC_GELU_P_LEAD, MPC_GELU_P_LEAD);
 #define MPC_HORNER2(c) p = fma2(p, u, pk(c, c));
-  MPC_GELU_P(MPC_HORNER2)
+  MPC_GELU_P_REST(MPC_HORNER2)
 #undef MPC_HORNER2
   const unsigned long long hi = mul2(t, t);
   const float2 hf = unpk(hi);
