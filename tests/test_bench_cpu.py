@@ -21,7 +21,7 @@ def reference_line(*extra):
     return json.loads(lines[0])
 
 
-@pytest.mark.parametrize("extra", [("--workload", "batched_gemm_bf16"),
+@pytest.mark.parametrize("extra", [("--workload", "batched_gemm_bf16"), ("--workload", "gpt2_attention_bf16"),
                                    ("--workload", "fused_elementwise_f32"),
                                    ("--workload", "fused_elementwise_f32", "--expression", "gelu_chain",
                                     "--precision", "f32")])
