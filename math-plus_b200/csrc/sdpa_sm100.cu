@@ -17,9 +17,9 @@
 //   warps 10-11      idle (they complete the load / MMA warpgroup for register reconfiguration)
 //   issue order per KV tile j: QK(1,j), PV(0,j), QK(0,j+1), PV(1,j), so each Q tile's softmax runs
 //   while the tensor core works on the other tile. For causal launches over at most 1024 keys
-//   warp 10 issues Q tile 1's MMAs and warp 9 only tile 0's, each in its own order QK(t,j),
-//   PV(t,j), QK(t,j+1). Causal: KV tiles past a Q tile's diagonal are skipped, only diagonal tiles
-//   are masked element-wise.
+//   (1536 at head dim 64) warp 10 issues Q tile 1's MMAs and warp 9 only tile 0's, each in its
+//   own order QK(t,j), PV(t,j), QK(t,j+1). Causal: KV tiles past a Q tile's diagonal are skipped,
+//   only diagonal tiles are masked element-wise.
 //   TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D).
 // Generic path (any head dim <= 256, f32 / f16 / bf16, any alignment): one warp per query row on the
 // CUDA cores, online softmax in f32 — the role of backend-webgpu's generic sdpa kernel.
@@ -162,8 +162,8 @@ __global__ void __launch_bounds__(384, 1) attn_kernel(const __grid_constant__ Ma
   // DUAL: each Q tile's MMAs come from their own thread (warps 9 and 10), so that one tile's QK and
   // PV follow its own softmax instead of waiting in one in-order stream behind the other tile's,
   // and a tile that finishes a unit early moves on to the next one. The host picks it for causal
-  // launches over at most 1024 keys, where unit boundaries are frequent; over longer or
-  // non-causal rows the single interleaved stream measured faster.
+  // launches over at most 1024 keys (1536 at head dim 64), where unit boundaries are frequent or
+  // the softmax dominates; over longer or non-causal rows the single stream measured faster.
   constexpr bool kDualIssue = DUAL;
   constexpr int kIssuers = kDualIssue ? 2 : 1;
 
@@ -710,8 +710,9 @@ int launch_order(mpc_device *dev, const Maps &maps, const Params &p, long long g
 // the MMA issuers are separate instantiations, so that no kernel carries a branch for the others.
 // Measured (causal, A/B on one box each time): [8,16,1024,128] bf16 383-422 TFLOP/s with one
 // issuer per tile against 364-369 with one stream; [16,16,512,128] f16 318 against 292-313;
-// [32,12,1024,64] f16 306-314 against 293-301; [16,32,2048,128] f16 707 against 814 and
-// non-causal rows 756-774 against 873-1009, so those keep the one stream.
+// [32,12,1024,64] f16 306-314 against 293-301; [32,12,1536,64] bf16 307-314 against 293-302; but
+// [16,32,1280,128] f16 625 against 664, [16,32,1536,128] f16 658 against 704, [16,32,2048,128] f16
+// 707 against 814 and non-causal rows 756-774 against 873-1009, so those keep the one stream.
 template <int D, bool BF>
 int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
   const long long sms = dev->prop.multiProcessorCount;
@@ -720,7 +721,7 @@ int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t s
   const long long grid_snake = p.n_units < sms ? p.n_units : sms;
   if (!p.causal) return launch_order<D, BF, false, false>(dev, maps, p, grid, st);
   const bool snake = prefer_snake(p, grid, grid_snake);
-  if (p.Lk <= 1024)
+  if (p.Lk <= (D == 64 ? 1536 : 1024))
     return snake ? launch_order<D, BF, true, true>(dev, maps, p, grid_snake, st)
                  : launch_order<D, BF, false, true>(dev, maps, p, grid, st);
   return snake ? launch_order<D, BF, true, false>(dev, maps, p, grid_snake, st)
