@@ -712,7 +712,8 @@ int launch_order(mpc_device *dev, const Maps &maps, const Params &p, long long g
 // issuer per tile against 364-369 with one stream; [16,16,512,128] f16 318 against 292-313;
 // [32,12,1024,64] f16 306-314 against 293-301; [32,12,1536,64] bf16 307-314 against 293-302; but
 // [16,32,1280,128] f16 625 against 664, [16,32,1536,128] f16 658 against 704, [16,32,2048,128] f16
-// 707 against 814 and non-causal rows 756-774 against 873-1009, so those keep the one stream.
+// 707 against 814, [16,12,2048,64] bf16 361 against 382, [8,12,4096,64] bf16 394 against 443, and
+// non-causal rows 756-774 against 873-1009, so those keep the one stream.
 template <int D, bool BF>
 int launch_tc(mpc_device *dev, const Maps &maps, const Params &p, cudaStream_t st) {
   const long long sms = dev->prop.multiProcessorCount;
